@@ -1,0 +1,16 @@
+// Kernel instantiations for element type __nv_bfloat16.
+#include "dynconv_launch.cuh"
+
+namespace greta {
+
+cudaError_t launch_fwd_bf16(const FwdParams& p, int nv, int norm, int gv, const LaunchShape& s,
+                         cudaStream_t st) {
+  return launch_fwd<__nv_bfloat16>(p, nv, norm, gv, s, st);
+}
+
+cudaError_t launch_bwd_bf16(const BwdParams& p, int nv, int norm, int gv, const LaunchShape& s,
+                         cudaStream_t st) {
+  return launch_bwd<__nv_bfloat16>(p, nv, norm, gv, s, st);
+}
+
+}  // namespace greta

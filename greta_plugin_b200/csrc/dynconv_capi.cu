@@ -1,0 +1,268 @@
+// C ABI of libgreta_dynconv.so: argument validation, vector-path selection,
+// launch shapes, and dispatch to the per-dtype kernel instantiations.
+// Declarations and the contract of every entry point: include/greta_dynconv.h.
+#include <stdint.h>
+
+#include <climits>
+#include <initializer_list>
+
+#include "dynconv_launch.cuh"
+#include "greta_dynconv.h"
+
+using namespace greta;
+
+namespace {
+
+constexpr int kAbiVersion = 10000;  // 1.0.0
+
+int esize(int dtype) {
+  switch (dtype) {
+    case GRETA_DT_F32: return 4;
+    case GRETA_DT_F16: return 2;
+    case GRETA_DT_BF16: return 2;
+    default: return 0;
+  }
+}
+
+bool is_pow2(int64_t v) { return v > 0 && (v & (v - 1)) == 0; }
+
+bool aligned(const void* p, int64_t a) { return p == nullptr || (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+int check_common(int dtype, int64_t D, int64_t W, int64_t G, int norm) {
+  if (esize(dtype) == 0) return GRETA_ERR_UNSUPPORTED;
+  if (D <= 0 || W <= 0 || G <= 0) return GRETA_ERR_INVALID_ARG;
+  if (D > (int64_t)INT_MAX / 2) return GRETA_ERR_INVALID_ARG;
+  if (D % G != 0) return GRETA_ERR_INVALID_ARG;
+  if (!is_pow2(G) || G > 256) return GRETA_ERR_UNSUPPORTED;
+  if (W > kMaxWGeneric) return GRETA_ERR_UNSUPPORTED;
+  if (norm < GRETA_NORM_NONE || norm > GRETA_NORM_STABLE) return GRETA_ERR_UNSUPPORTED;
+  return GRETA_OK;
+}
+
+int group_vec(int nv, int64_t G) { return nv == 1 ? 1 : (G >= kVec ? 1 : (int)(kVec / G)); }
+
+// kVec channels per thread when every row is a whole number of aligned
+// vectors; one channel per thread otherwise (only possible for G <= 32,
+// since one group must fit the lanes of one warp).
+int pick_nv(int dtype, int64_t D, int64_t G, std::initializer_list<const void*> rows, const void* w) {
+  const int es = esize(dtype);
+  bool ok = D % kVec == 0;
+  for (const void* p : rows) ok = ok && aligned(p, (int64_t)kVec * es);
+  ok = ok && aligned(w, (int64_t)group_vec(kVec, G) * es);
+  if (ok) return kVec;
+  if (G > 32) return 0;
+  return 1;
+}
+
+LaunchShape make_shape(long long chunks, int64_t D, int nv, int tx, int ty) {
+  const long long lanes = (D + nv - 1) / nv;
+  const long long need = ((lanes + 31) / 32) * 32;
+  if (tx > need) tx = (int)need;
+  LaunchShape s;
+  s.block = dim3(tx, ty, 1);
+  s.grid = dim3((unsigned)chunks, (unsigned)((lanes + tx - 1) / tx), 1);
+  return s;
+}
+
+int finish(cudaError_t e) { return e == cudaSuccess ? GRETA_OK : GRETA_ERR_LAUNCH; }
+
+cudaError_t run_fwd(int dtype, const FwdParams& p, int nv, int norm, const LaunchShape& s, void* stream) {
+  const int gv = group_vec(nv, p.G);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case GRETA_DT_F32: return launch_fwd_f32(p, nv, norm, gv, s, st);
+    case GRETA_DT_F16: return launch_fwd_f16(p, nv, norm, gv, s, st);
+    default: return launch_fwd_bf16(p, nv, norm, gv, s, st);
+  }
+}
+
+cudaError_t run_bwd(int dtype, const BwdParams& p, int nv, int norm, const LaunchShape& s, void* stream) {
+  const int gv = group_vec(nv, p.G);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case GRETA_DT_F32: return launch_bwd_f32(p, nv, norm, gv, s, st);
+    case GRETA_DT_F16: return launch_bwd_f16(p, nv, norm, gv, s, st);
+    default: return launch_bwd_bf16(p, nv, norm, gv, s, st);
+  }
+}
+
+long long cdiv(long long a, long long b) { return (a + b - 1) / b; }
+
+}  // namespace
+
+extern "C" {
+
+int greta_dynconv_fwd(int dtype, const void* x, const void* w, const void* gate, void* y, void* yr,
+                      const void* cu_seqlens, int cu_seqlens_int64, int64_t num_seqs, int64_t T,
+                      int64_t D, int64_t W, int64_t G, int norm, float eps, void* stream) {
+  int rc = check_common(dtype, D, W, G, norm);
+  if (rc) return rc;
+  if (!x || !w || !y || T < 0 || (cu_seqlens && num_seqs < 0)) return GRETA_ERR_INVALID_ARG;
+  if (T == 0 || (cu_seqlens && num_seqs == 0)) return GRETA_OK;
+  const int nv = pick_nv(dtype, D, G, {x, gate, y, yr}, w);
+  if (nv == 0) return GRETA_ERR_ALIGNMENT;
+  const int H = (int)W - 1;
+  const int ty = 4;
+  const int L = H > 16 ? H : 16;
+  FwdParams p{};
+  p.x = x; p.w = w; p.g = gate; p.y = y; p.yr = norm != GRETA_NORM_NONE ? yr : nullptr;
+  p.starts = cu_seqlens; p.starts_i64 = cu_seqlens_int64 ? 1 : 0;
+  p.mode = cu_seqlens ? kModePacked : kModeSingle;
+  p.nseq = cu_seqlens ? num_seqs : 1;
+  p.T = T; p.D = (int)D; p.W = (int)W; p.G = (int)G;
+  p.L = L; p.chunk = L * ty;
+  p.eps = eps;
+  const long long chunks = cdiv(T, p.chunk) + (cu_seqlens ? num_seqs : 0);
+  if (chunks > INT_MAX) return GRETA_ERR_INVALID_ARG;
+  return finish(run_fwd(dtype, p, nv, norm, make_shape(chunks, D, nv, 32, ty), stream));
+}
+
+int greta_dynconv_bwd(int dtype, const void* x, const void* w, const void* gate, const void* yr,
+                      const void* dout, void* dx, void* dw, void* dg, const void* cu_seqlens,
+                      int cu_seqlens_int64, int64_t num_seqs, int64_t T, int64_t D, int64_t W,
+                      int64_t G, int norm, float eps, void* stream) {
+  int rc = check_common(dtype, D, W, G, norm);
+  if (rc) return rc;
+  if (norm == GRETA_NORM_STABLE) return GRETA_ERR_UNSUPPORTED;
+  if (!x || !w || !dout || !dx || !dw || T < 0 || (cu_seqlens && num_seqs < 0)) return GRETA_ERR_INVALID_ARG;
+  if ((gate == nullptr) != (dg == nullptr)) return GRETA_ERR_INVALID_ARG;
+  if (norm != GRETA_NORM_NONE && yr == nullptr) return GRETA_ERR_INVALID_ARG;
+  if (T == 0 || (cu_seqlens && num_seqs == 0)) return GRETA_OK;
+  int nv = pick_nv(dtype, D, G, {x, gate, yr, dout, dx, dg}, w);
+  if (nv == kVec && !aligned(dw, (int64_t)group_vec(kVec, G) * esize(dtype))) nv = G > 32 ? 0 : 1;
+  if (nv == 0) return GRETA_ERR_ALIGNMENT;
+  const int H = (int)W - 1;
+  const int ty = 4;
+  const int L = H > 32 ? H : 32;
+  BwdParams p{};
+  p.x = x; p.w = w; p.g = gate; p.yr = norm != GRETA_NORM_NONE ? yr : nullptr; p.dout = dout;
+  p.dx = dx; p.dw = dw; p.dg = dg;
+  p.starts = cu_seqlens; p.starts_i64 = cu_seqlens_int64 ? 1 : 0;
+  p.mode = cu_seqlens ? kModePacked : kModeSingle;
+  p.nseq = cu_seqlens ? num_seqs : 1;
+  p.T = T; p.D = (int)D; p.W = (int)W; p.G = (int)G;
+  p.L = L; p.chunk = L * ty;
+  p.eps = eps;
+  const long long chunks = cdiv(T, p.chunk) + (cu_seqlens ? num_seqs : 0);
+  if (chunks > INT_MAX) return GRETA_ERR_INVALID_ARG;
+  return finish(run_bwd(dtype, p, nv, norm, make_shape(chunks, D, nv, 32, ty), stream));
+}
+
+int greta_dynconv_inference(int dtype, const void* context, const void* w, const void* gate, void* y,
+                            int64_t B, int64_t Q, int64_t D, int64_t W, int64_t G, int norm, float eps,
+                            void* stream) {
+  int rc = check_common(dtype, D, W, G, norm);
+  if (rc) return rc;
+  if (!context || !w || !y || B < 0 || Q < 0) return GRETA_ERR_INVALID_ARG;
+  if (B == 0 || Q == 0) return GRETA_OK;
+  const int nv = pick_nv(dtype, D, G, {context, gate, y}, w);
+  if (nv == 0) return GRETA_ERR_ALIGNMENT;
+  const int H = (int)W - 1;
+  const int ty = 4;
+  const int L = H > 16 ? H : 16;
+  FwdParams p{};
+  p.x = context; p.w = w; p.g = gate; p.y = y; p.yr = nullptr;
+  p.mode = kModeContext;
+  p.nseq = B;
+  p.T = Q; p.D = (int)D; p.W = (int)W; p.G = (int)G;
+  p.L = L; p.chunk = L * ty;
+  p.eps = eps;
+  const long long chunks = B * cdiv(Q, p.chunk);
+  if (chunks > INT_MAX) return GRETA_ERR_INVALID_ARG;
+  return finish(run_fwd(dtype, p, nv, norm, make_shape(chunks, D, nv, 32, ty), stream));
+}
+
+int greta_dynconv_decode_rows(int dtype, const void* x, const void* w, const void* gate, void* conv_state,
+                              void* y, int64_t B, int64_t D, int64_t W, int64_t G, int norm, float eps,
+                              void* stream) {
+  int rc = check_common(dtype, D, W, G, norm);
+  if (rc) return rc;
+  if (!x || !w || !conv_state || !y || B < 0 || W < 2) return GRETA_ERR_INVALID_ARG;
+  if (B == 0) return GRETA_OK;
+  if (B > INT_MAX) return GRETA_ERR_INVALID_ARG;
+  const int nv = pick_nv(dtype, D, G, {x, gate, y}, w);
+  if (nv == 0) return GRETA_ERR_ALIGNMENT;
+  const int H = (int)W - 1;
+  const int es = esize(dtype);
+  FwdParams p{};
+  p.x = x; p.w = w; p.g = gate; p.y = y; p.yr = nullptr;
+  p.mode = kModeRows;
+  p.nseq = B;
+  p.T = B; p.D = (int)D; p.W = (int)W; p.G = (int)G;
+  p.L = H; p.chunk = H;
+  p.state = conv_state;
+  p.s_slot = D * H; p.s_d = H; p.s_h = 1; p.num_slots = B;
+  p.st_layout = (nv == kVec && aligned(conv_state, (int64_t)kVec * es)) ? kStDS : kStGeneric;
+  p.eps = eps;
+  return finish(run_fwd(dtype, p, nv, norm, make_shape(B, D, nv, 128, 1), stream));
+}
+
+int greta_dynconv_packed_state(int dtype, const void* x, const void* w, const void* gate, void* y,
+                               void* state, int64_t num_slots, int64_t s_slot, int64_t s_d, int64_t s_h,
+                               const int32_t* starts, const int32_t* slots, const int8_t* has_initial,
+                               int64_t num_reqs, int64_t T, int64_t D, int64_t W, int64_t G, int norm,
+                               float eps, int32_t* error_flags, void* stream) {
+  int rc = check_common(dtype, D, W, G, norm);
+  if (rc) return rc;
+  const int H = (int)W - 1;
+  if (!x || !w || !y || !starts || !slots || !has_initial || T < 0 || num_reqs < 0 || num_slots < 0)
+    return GRETA_ERR_INVALID_ARG;
+  if (H > 0 && !state && num_slots > 0) return GRETA_ERR_INVALID_ARG;
+  if (T == 0 || num_reqs == 0) return GRETA_OK;
+  const int nv = pick_nv(dtype, D, G, {x, gate, y}, w);
+  if (nv == 0) return GRETA_ERR_ALIGNMENT;
+  const int es = esize(dtype);
+  const bool decode_like = T <= 2 * num_reqs;
+  const int ty = decode_like ? 1 : 4;
+  int L = decode_like ? 4 : 8;
+  if (L < H) L = H;
+  FwdParams p{};
+  p.x = x; p.w = w; p.g = gate; p.y = y; p.yr = nullptr;
+  p.starts = starts; p.starts_i64 = 0;
+  p.mode = kModePacked;
+  p.nseq = num_reqs;
+  p.T = T; p.D = (int)D; p.W = (int)W; p.G = (int)G;
+  p.L = L; p.chunk = L * ty;
+  p.slots = slots;
+  p.initial = reinterpret_cast<const signed char*>(has_initial);
+  p.err = error_flags;
+  p.eps = eps;
+  if (H > 0 && state != nullptr && num_slots > 0) {
+    p.state = state;
+    p.s_slot = s_slot; p.s_d = s_d; p.s_h = s_h; p.num_slots = num_slots;
+    const bool base_ok = nv == kVec && aligned(state, (int64_t)kVec * es) && s_slot % kVec == 0;
+    if (base_ok && s_h == 1 && s_d == H)
+      p.st_layout = kStDS;
+    else if (base_ok && s_d == 1 && s_h % kVec == 0)
+      p.st_layout = kStSD;
+    else
+      p.st_layout = kStGeneric;
+  } else {
+    // No history storage (W == 1, or an empty cache): every slot reads as
+    // "no history" and nothing is written back.
+    p.state = nullptr;
+    p.num_slots = 0;
+  }
+  const long long chunks = cdiv(T, p.chunk) + num_reqs;
+  if (chunks > INT_MAX) return GRETA_ERR_INVALID_ARG;
+  return finish(run_fwd(dtype, p, nv, norm, make_shape(chunks, D, nv, decode_like ? 128 : 32, ty), stream));
+}
+
+int greta_dynconv_supports(int64_t group_size, int64_t channels) {
+  return (is_pow2(group_size) && group_size <= 256 && channels > 0 && channels % group_size == 0) ? 1 : 0;
+}
+
+const char* greta_dynconv_status_string(int status) {
+  switch (status) {
+    case GRETA_OK: return "ok";
+    case GRETA_ERR_INVALID_ARG: return "invalid argument (null pointer, negative size or shape mismatch)";
+    case GRETA_ERR_UNSUPPORTED: return "unsupported configuration (dtype, group size, kernel size or norm kind)";
+    case GRETA_ERR_ALIGNMENT: return "misaligned pointer for the vector path with group size > 32";
+    case GRETA_ERR_LAUNCH: return "CUDA kernel launch failed";
+    default: return "unknown status";
+  }
+}
+
+int greta_dynconv_version(void) { return kAbiVersion; }
+
+}  // extern "C"

@@ -1,0 +1,316 @@
+// Shared device code for the dynamic causal depthwise convolution kernels.
+//
+// Work decomposition (all kernels):
+//   grid.x  = chunks: a chunk is a run of consecutive tokens of ONE sequence
+//             (sequence = packed request, cu_seqlens segment, batch row).
+//   grid.y  = channel blocks of blockDim.x * NV channels.
+//   thread  = NV consecutive channels (one 16-byte vector for 16-bit types)
+//             x a run of L consecutive tokens; threadIdx.y picks the run
+//             inside the chunk. A thread walks its run in time order and
+//             keeps the last W-1 inputs in registers, so every x row is read
+//             once from HBM (plus a W-1 row halo per run, which hits L1/L2).
+//
+// Sequences are resolved on the device from the cumulative offsets (no host
+// chunk table, no host synchronisation): each CTA scans the per-sequence chunk
+// counts with a block-wide prefix sum and finds its (sequence, chunk) pair.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace greta {
+
+constexpr int kVec = 8;          // channels per thread on the vector path
+constexpr int kMaxWGeneric = 16; // largest kernel size handled by the generic-W variant
+
+enum NormKind { kNormNone = 0, kNormPlain = 1, kNormStable = 2 };
+enum SeqMode { kModeSingle = 0, kModePacked = 1, kModeContext = 2, kModeRows = 3 };
+enum HistKind { kHistZero = 0, kHistX = 1, kHistState = 2 };
+enum StateLayout { kStGeneric = 0, kStDS = 1, kStSD = 2 };
+
+// Parameters of the forward family (training fwd, HF inference, HF decode,
+// vLLM packed conv + state write-back).
+struct FwdParams {
+  const void* x;   // [rows, D]
+  const void* w;   // [out rows, W, D/G]
+  const void* g;   // [out rows, D] or null
+  void* y;         // [out rows, D]
+  void* yr;        // [out rows, D] or null (pre-norm output)
+  const void* starts;  // [nseq + 1] (PACKED) or null
+  int starts_i64;
+  int mode;            // SeqMode
+  long long nseq;      // sequences (PACKED) or batch rows (CONTEXT / ROWS)
+  long long T;         // total tokens (SINGLE / PACKED) or Q (CONTEXT)
+  int D, W, G;
+  int L;               // tokens per thread run
+  int chunk;           // tokens per CTA = L * blockDim.y
+  // cache-slot state
+  void* state;         // null = no state
+  long long s_slot, s_d, s_h, num_slots;
+  int st_layout;       // StateLayout
+  const int* slots;    // [nseq] or null (ROWS: slot = row)
+  const signed char* initial;  // [nseq] or null
+  int* err;            // device error bits or null
+  float eps;
+};
+
+struct BwdParams {
+  const void* x;
+  const void* w;
+  const void* g;
+  const void* yr;
+  const void* dout;
+  void* dx;
+  void* dw;
+  void* dg;
+  const void* starts;
+  int starts_i64;
+  int mode;  // SINGLE or PACKED
+  long long nseq;
+  long long T;
+  int D, W, G;
+  int L;
+  int chunk;
+  float eps;
+};
+
+// ---------------------------------------------------------------------------
+// element packs and conversions
+// ---------------------------------------------------------------------------
+template <typename T, int N>
+struct alignas(sizeof(T) * N) Pack {
+  T v[N];
+};
+
+__device__ __forceinline__ float to_f(float v) { return v; }
+__device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
+__device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+template <typename T>
+__device__ __forceinline__ T from_f(float v);
+template <>
+__device__ __forceinline__ float from_f<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ __half from_f<__half>(float v) { return __float2half_rn(v); }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float v) {
+  return __float2bfloat16_rn(v);
+}
+
+template <typename T, int N>
+__device__ __forceinline__ void zero(Pack<T, N>& p) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) p.v[i] = from_f<T>(0.f);
+}
+
+template <typename T, int N>
+__device__ __forceinline__ Pack<T, N> ld(const T* ptr) {
+  return *reinterpret_cast<const Pack<T, N>*>(ptr);
+}
+
+template <typename T, int N>
+__device__ __forceinline__ void st(T* ptr, const Pack<T, N>& v) {
+  *reinterpret_cast<Pack<T, N>*>(ptr) = v;
+}
+
+// Runtime-indexed read of a small register array without local memory.
+template <int N, typename P>
+__device__ __forceinline__ P sel(const P (&a)[N], int idx) {
+  P r = a[0];
+#pragma unroll
+  for (int k = 1; k < N; ++k)
+    if (k == idx) r = a[k];
+  return r;
+}
+
+__device__ __forceinline__ float sigmoidf_(float v) { return 1.f / (1.f + __expf(-v)); }
+
+// ---------------------------------------------------------------------------
+// group reductions. NV channels per thread; GV groups per thread when G < NV
+// (GC = NV / GV channels each), else one group spread over lpg = G / NV lanes.
+// ---------------------------------------------------------------------------
+template <int NV, int GV>
+__device__ __forceinline__ void group_sum(const float (&v)[NV], float (&out)[GV], int lpg) {
+  constexpr int GC = NV / GV;
+#pragma unroll
+  for (int gi = 0; gi < GV; ++gi) {
+    float s = 0.f;
+#pragma unroll
+    for (int c = 0; c < GC; ++c) s += v[gi * GC + c];
+    out[gi] = s;
+  }
+  if (GV == 1) {
+    for (int o = 1; o < lpg; o <<= 1) out[0] += __shfl_xor_sync(0xffffffffu, out[0], o);
+  }
+}
+
+template <int NV, int GV>
+__device__ __forceinline__ void group_max(const float (&v)[NV], float (&out)[GV], int lpg) {
+  constexpr int GC = NV / GV;
+#pragma unroll
+  for (int gi = 0; gi < GV; ++gi) {
+    float s = v[gi * GC];
+#pragma unroll
+    for (int c = 1; c < GC; ++c) s = fmaxf(s, v[gi * GC + c]);
+    out[gi] = s;
+  }
+  if (GV == 1) {
+    for (int o = 1; o < lpg; o <<= 1) out[0] = fmaxf(out[0], __shfl_xor_sync(0xffffffffu, out[0], o));
+  }
+}
+
+// Group RMS norm of a thread's NV accumulators, in place.
+//   plain : y * 1/sqrt(mean(y^2) + eps)               (greta/dynamic_conv.py:251-255)
+//   stable: s = max(max|y|, 1); y / (s * sqrt(mean((y/s)^2) + eps/s^2))
+//                                                    (greta_vllm/triton_conv.py:71-77)
+template <int NORM, int NV, int GV>
+__device__ __forceinline__ void apply_norm(float (&acc)[NV], int G, int lpg, float eps) {
+  constexpr int GC = NV / GV;
+  const float inv_g = 1.f / (float)G;  // G is a power of two: exact
+  if (NORM == kNormPlain) {
+    float sq[NV], ss[GV];
+#pragma unroll
+    for (int c = 0; c < NV; ++c) sq[c] = acc[c] * acc[c];
+    group_sum<NV, GV>(sq, ss, lpg);
+#pragma unroll
+    for (int gi = 0; gi < GV; ++gi) ss[gi] = 1.f / sqrtf(ss[gi] * inv_g + eps);
+#pragma unroll
+    for (int c = 0; c < NV; ++c) acc[c] *= ss[c / GC];
+  } else if (NORM == kNormStable) {
+    float ab[NV], mx[GV];
+#pragma unroll
+    for (int c = 0; c < NV; ++c) ab[c] = fabsf(acc[c]);
+    group_max<NV, GV>(ab, mx, lpg);
+#pragma unroll
+    for (int gi = 0; gi < GV; ++gi) mx[gi] = fmaxf(mx[gi], 1.f);
+    float sq[NV], ss[GV];
+#pragma unroll
+    for (int c = 0; c < NV; ++c) {
+      const float s = acc[c] / mx[c / GC];
+      sq[c] = s * s;
+    }
+    group_sum<NV, GV>(sq, ss, lpg);
+#pragma unroll
+    for (int gi = 0; gi < GV; ++gi)
+      ss[gi] = mx[gi] * sqrtf(ss[gi] * inv_g + eps / (mx[gi] * mx[gi]));
+#pragma unroll
+    for (int c = 0; c < NV; ++c) acc[c] = acc[c] / ss[c / GC];
+  }
+}
+
+// ---------------------------------------------------------------------------
+// chunk resolution
+// ---------------------------------------------------------------------------
+struct ChunkInfo {
+  long long x_base;  // row of local position 0 in x
+  long long o_base;  // row of local position 0 in w / g / y / yr
+  long long len;     // sequence length
+  long long c0, c1;  // chunk token range [c0, c1), local positions
+  long long slot;    // cache slot, -1 = none
+  int hist;          // HistKind for positions < 0
+  int has_state;     // old slot contents are used
+  int head;          // first chunk of its sequence
+};
+
+__device__ __forceinline__ long long load_idx(const void* p, long long i, int is64) {
+  return is64 ? reinterpret_cast<const long long*>(p)[i] : (long long)reinterpret_cast<const int*>(p)[i];
+}
+
+__device__ __forceinline__ long long clampll(long long v, long long lo, long long hi) {
+  return v < lo ? lo : (v > hi ? hi : v);
+}
+
+// Block-wide search of chunk `cid` among sequences described by cumulative
+// offsets `starts` (clamped to [0, T]). Sequence i owns max(1, ceil(len_i /
+// chunk)) chunks (an empty sequence keeps one chunk for its state write-back).
+// All threads of the block must call this. Returns false when cid is past the
+// last chunk. Each thread handles kItems consecutive sequences per pass.
+struct SeqHit {
+  long long s, j, a, b;
+  int slot_raw;
+  int init;
+};
+
+template <int kItems>
+__device__ bool block_find_chunk(const void* starts, int is64, long long nseq, long long T,
+                                 int chunk, long long cid, const int* slots,
+                                 const signed char* initial, SeqHit& hit) {
+  __shared__ long long sh_warp[32];
+  __shared__ SeqHit sh_hit;
+  __shared__ int sh_found;
+  const int nthr = blockDim.x * blockDim.y;
+  const int tid = threadIdx.y * blockDim.x + threadIdx.x;
+  const int lane = tid & 31, wid = tid >> 5, nw = (nthr + 31) >> 5;
+  if (tid == 0) sh_found = 0;
+  __syncthreads();
+  long long running = 0;
+  for (long long base = 0; base < nseq; base += (long long)nthr * kItems) {
+    const long long i0 = base + (long long)tid * kItems;
+    long long bnd[kItems + 1];
+    long long cnt[kItems];
+    long long tot = 0;
+#pragma unroll
+    for (int k = 0; k <= kItems; ++k) {
+      const long long i = i0 + k;
+      bnd[k] = (i <= nseq) ? clampll(load_idx(starts, i, is64), 0, T) : 0;
+    }
+#pragma unroll
+    for (int k = 0; k < kItems; ++k) {
+      long long n = 0;
+      if (i0 + k < nseq) {
+        n = bnd[k + 1] - bnd[k];
+        if (n < 0) n = 0;
+        n = n > 0 ? (n + chunk - 1) / chunk : 1;
+      }
+      cnt[k] = n;
+      tot += n;
+    }
+    // block exclusive scan of tot
+    long long incl = tot;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const long long t = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += t;
+    }
+    if (lane == 31 || tid == nthr - 1) sh_warp[wid] = incl;
+    __syncthreads();
+    if (wid == 0) {
+      long long v = lane < nw ? sh_warp[lane] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const long long t = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += t;
+      }
+      if (lane < nw) sh_warp[lane] = v;
+    }
+    __syncthreads();
+    long long ex = running + (wid > 0 ? sh_warp[wid - 1] : 0) + incl - tot;
+    const long long block_total = sh_warp[nw - 1];
+#pragma unroll
+    for (int k = 0; k < kItems; ++k) {
+      if (i0 + k < nseq && cid >= ex && cid < ex + cnt[k]) {
+        SeqHit h;
+        h.s = i0 + k;
+        h.j = cid - ex;
+        h.a = bnd[k];
+        h.b = bnd[k + 1] < bnd[k] ? bnd[k] : bnd[k + 1];
+        h.slot_raw = slots ? slots[i0 + k] : -1;
+        h.init = initial ? (int)initial[i0 + k] : 0;
+        sh_hit = h;
+        sh_found = 1;
+      }
+      ex += cnt[k];
+    }
+    running += block_total;
+    __syncthreads();
+    if (running > cid) break;  // uniform: running is the same in every thread
+  }
+  const bool found = sh_found != 0;
+  if (found) hit = sh_hit;
+  return found;
+}
+
+}  // namespace greta
+

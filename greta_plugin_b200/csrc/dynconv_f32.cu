@@ -1,0 +1,16 @@
+// Kernel instantiations for element type float.
+#include "dynconv_launch.cuh"
+
+namespace greta {
+
+cudaError_t launch_fwd_f32(const FwdParams& p, int nv, int norm, int gv, const LaunchShape& s,
+                         cudaStream_t st) {
+  return launch_fwd<float>(p, nv, norm, gv, s, st);
+}
+
+cudaError_t launch_bwd_f32(const BwdParams& p, int nv, int norm, int gv, const LaunchShape& s,
+                         cudaStream_t st) {
+  return launch_bwd<float>(p, nv, norm, gv, s, st);
+}
+
+}  // namespace greta

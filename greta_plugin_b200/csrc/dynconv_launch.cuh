@@ -1,0 +1,102 @@
+// Compile-time dispatch from runtime (NV, W, norm, GV) to a kernel
+// instantiation. The W template argument is the exact kernel size when > 0
+// (the common W = 4 and W = 7), or -MAXW for a runtime W <= MAXW. Included once per element type (dynconv_<dtype>.cu) so the
+// three element types compile in parallel.
+#pragma once
+
+#include "dynconv_bwd.cuh"
+#include "dynconv_fwd.cuh"
+
+namespace greta {
+
+struct LaunchShape {
+  dim3 grid;
+  dim3 block;
+};
+
+template <typename T, int NV, int WT, int NORM>
+cudaError_t fwd_gv(const FwdParams& p, int gv, const LaunchShape& s, cudaStream_t st) {
+  if constexpr (NV == kVec) {
+    switch (gv) {
+      case 8: dynconv_fwd_kernel<T, NV, WT, NORM, 8><<<s.grid, s.block, 0, st>>>(p); break;
+      case 4: dynconv_fwd_kernel<T, NV, WT, NORM, 4><<<s.grid, s.block, 0, st>>>(p); break;
+      case 2: dynconv_fwd_kernel<T, NV, WT, NORM, 2><<<s.grid, s.block, 0, st>>>(p); break;
+      case 1: dynconv_fwd_kernel<T, NV, WT, NORM, 1><<<s.grid, s.block, 0, st>>>(p); break;
+      default: return cudaErrorInvalidValue;
+    }
+  } else {
+    if (gv != 1) return cudaErrorInvalidValue;
+    dynconv_fwd_kernel<T, NV, WT, NORM, 1><<<s.grid, s.block, 0, st>>>(p);
+  }
+  return cudaGetLastError();
+}
+
+template <typename T, int NV, int WT>
+cudaError_t fwd_norm(const FwdParams& p, int norm, int gv, const LaunchShape& s, cudaStream_t st) {
+  switch (norm) {
+    case kNormNone: return fwd_gv<T, NV, WT, kNormNone>(p, gv, s, st);
+    case kNormPlain: return fwd_gv<T, NV, WT, kNormPlain>(p, gv, s, st);
+    case kNormStable: return fwd_gv<T, NV, WT, kNormStable>(p, gv, s, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+template <typename T>
+cudaError_t launch_fwd(const FwdParams& p, int nv, int norm, int gv, const LaunchShape& s,
+                       cudaStream_t st) {
+  if (nv == kVec) {
+    if (p.W == 4) return fwd_norm<T, kVec, 4>(p, norm, gv, s, st);
+    if (p.W == 7) return fwd_norm<T, kVec, 7>(p, norm, gv, s, st);
+    if (p.W <= 8) return fwd_norm<T, kVec, -8>(p, norm, gv, s, st);
+    return fwd_norm<T, kVec, -kMaxWGeneric>(p, norm, gv, s, st);
+  }
+  return fwd_norm<T, 1, -kMaxWGeneric>(p, norm, gv, s, st);
+}
+
+template <typename T, int NV, int WT, int NORM>
+cudaError_t bwd_gv(const BwdParams& p, int gv, const LaunchShape& s, cudaStream_t st) {
+  if constexpr (NV == kVec) {
+    switch (gv) {
+      case 8: dynconv_bwd_kernel<T, NV, WT, NORM, 8><<<s.grid, s.block, 0, st>>>(p); break;
+      case 4: dynconv_bwd_kernel<T, NV, WT, NORM, 4><<<s.grid, s.block, 0, st>>>(p); break;
+      case 2: dynconv_bwd_kernel<T, NV, WT, NORM, 2><<<s.grid, s.block, 0, st>>>(p); break;
+      case 1: dynconv_bwd_kernel<T, NV, WT, NORM, 1><<<s.grid, s.block, 0, st>>>(p); break;
+      default: return cudaErrorInvalidValue;
+    }
+  } else {
+    if (gv != 1) return cudaErrorInvalidValue;
+    dynconv_bwd_kernel<T, NV, WT, NORM, 1><<<s.grid, s.block, 0, st>>>(p);
+  }
+  return cudaGetLastError();
+}
+
+template <typename T, int NV, int WT>
+cudaError_t bwd_norm(const BwdParams& p, int norm, int gv, const LaunchShape& s, cudaStream_t st) {
+  switch (norm) {
+    case kNormNone: return bwd_gv<T, NV, WT, kNormNone>(p, gv, s, st);
+    case kNormPlain: return bwd_gv<T, NV, WT, kNormPlain>(p, gv, s, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+template <typename T>
+cudaError_t launch_bwd(const BwdParams& p, int nv, int norm, int gv, const LaunchShape& s,
+                       cudaStream_t st) {
+  if (nv == kVec) {
+    if (p.W == 4) return bwd_norm<T, kVec, 4>(p, norm, gv, s, st);
+    if (p.W == 7) return bwd_norm<T, kVec, 7>(p, norm, gv, s, st);
+    if (p.W <= 8) return bwd_norm<T, kVec, -8>(p, norm, gv, s, st);
+    return bwd_norm<T, kVec, -kMaxWGeneric>(p, norm, gv, s, st);
+  }
+  return bwd_norm<T, 1, -kMaxWGeneric>(p, norm, gv, s, st);
+}
+
+// Entry points defined by the per-dtype translation units.
+cudaError_t launch_fwd_f32(const FwdParams&, int, int, int, const LaunchShape&, cudaStream_t);
+cudaError_t launch_fwd_f16(const FwdParams&, int, int, int, const LaunchShape&, cudaStream_t);
+cudaError_t launch_fwd_bf16(const FwdParams&, int, int, int, const LaunchShape&, cudaStream_t);
+cudaError_t launch_bwd_f32(const BwdParams&, int, int, int, const LaunchShape&, cudaStream_t);
+cudaError_t launch_bwd_f16(const BwdParams&, int, int, int, const LaunchShape&, cudaStream_t);
+cudaError_t launch_bwd_bf16(const BwdParams&, int, int, int, const LaunchShape&, cudaStream_t);
+
+}  // namespace greta
