@@ -1,0 +1,578 @@
+"""Benchmark of the B200 dynamic causal depthwise convolution.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+                    [--workload prefill|decode|train|all] [--shard requests|channels]
+
+One JSON line on rank 0. The headline (`value`) is the varlen chunked prefill
+with cache-slot state: 8 sequences with lengths ~U[32, 256] packed to <= 1024
+tokens, C = 4096, K = 4, G = 1, bf16, state [64 slots, 4096, 3] read from 8
+distinct random slots and written back. The decode step (256 one-token
+requests, 1024 slots, 10% padding slots) and the training forward + backward
+(8 x 4096 packed tokens, C = 4096, K = 4) are reported under "workloads".
+
+Timing: W untimed warm-up steps, then exactly K steps between CUDA events on
+the launching stream, bracketed by a barrier and torch.cuda.synchronize();
+the time is the max over ranks. Prefill and decode inputs are smaller than
+L2, so each step reads the next of several rotating input sets (> 2x L2 in
+total) and the K launches are replayed from one CUDA graph. Training inputs
+are larger than L2.
+
+--impl reference times the reference algorithm on the host CPU cores (the
+restated oracle in oracle/, all threads) on the same workload; under torchrun
+only rank 0 runs it.
+
+Multi-GPU: one process per GPU. --shard requests (default, weak scaling):
+every rank serves its own batch of the same shape (no collective on the data
+path). --shard channels (strong scaling): the 4096 channels are split across
+ranks (column-parallel TP layout; no collective for the conv).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "dyn-conv tokens/s and % of B200 HBM peak (prefill fwd, train bwd, decode) at 1/2/4/8 GPUs"
+L2_BYTES = 126 * 2 ** 20
+FALLBACK_HBM_GBS = 6650.0
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def dram_traffic():
+    """Per-launch DRAM bytes of the kernels from a committed ncu summary."""
+    p = ROOT / "profiles" / "dram_traffic.json"
+    if p.exists():
+        return json.loads(p.read_text())
+    return {}
+
+
+# ---------------------------------------------------------------------------
+# clocks sampled during the timed work
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"greta_clocks_{os.getpid()}.csv"
+
+    def __enter__(self):
+        try:
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=self.fh, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.fh.close()
+
+    def summary(self):
+        if self.proc is None or not self.path.exists():
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        for line in self.path.read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append(dict(sm=float(parts[1]), smax=float(parts[2]), power=float(parts[3]),
+                                 hw=parts[5], hwt=parts[6], swt=parts[7], swp=parts[8]))
+            except ValueError:
+                continue
+        self.path.unlink(missing_ok=True)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        load = [r for r in rows if r["power"] > 250.0] or rows
+        reasons = sorted({name for r in load for name, key in (("hw_slowdown", "hw"),
+                                                                ("hw_thermal_slowdown", "hwt"),
+                                                                ("sw_thermal_slowdown", "swt"),
+                                                                ("sw_power_cap", "swp"))
+                          if r[key].lower() == "active"})
+        return {"sm_mhz": statistics.median(r["sm"] for r in load), "sm_max_mhz": max(r["smax"] for r in rows),
+                "reasons": reasons, "samples": len(rows), "samples_under_load": len(load)}
+
+
+# ---------------------------------------------------------------------------
+# workloads (synthetic, seeded, reference layouts)
+# ---------------------------------------------------------------------------
+def prefill_lengths(gen, torch):
+    while True:
+        lengths = torch.randint(32, 257, (8,), generator=gen).tolist()
+        if sum(lengths) <= 1024:
+            return lengths
+
+
+def make_prefill(torch, dev, seed, D=4096, W=4, G=1, n_slots=64):
+    g = torch.Generator().manual_seed(seed)
+    lengths = prefill_lengths(g, torch)
+    T = sum(lengths)
+    slots = torch.randperm(n_slots, generator=g)[:8].to(torch.int32)
+    gd = torch.Generator(device=dev).manual_seed(seed)
+    return dict(
+        x=torch.randn(T, D, device=dev, generator=gd).bfloat16(),
+        w=(torch.randn(T, W, D // G, device=dev, generator=gd) * (1.0 / W) ** 0.5).bfloat16(),
+        state=torch.randn(n_slots, D, W - 1, device=dev, generator=gd).bfloat16(),
+        starts=torch.tensor([0] + list(_cumsum(lengths)), dtype=torch.int32, device=dev),
+        slots=slots.to(dev), init=torch.ones(8, dtype=torch.int8, device=dev),
+        y=torch.empty(T, D, device=dev, dtype=torch.bfloat16), T=T, N=8, D=D, W=W, G=G, lengths=lengths)
+
+
+def make_decode(torch, dev, seed, D=4096, W=4, G=1, n_slots=1024, B=256):
+    g = torch.Generator().manual_seed(seed)
+    slots = torch.randperm(n_slots, generator=g)[:B]
+    pad = torch.randperm(B, generator=g)[: round(0.1 * B)]
+    slots[pad] = -1
+    gd = torch.Generator(device=dev).manual_seed(seed)
+    return dict(
+        x=torch.randn(B, D, device=dev, generator=gd).bfloat16(),
+        w=(torch.randn(B, W, D // G, device=dev, generator=gd) * (1.0 / W) ** 0.5).bfloat16(),
+        state=torch.randn(n_slots, D, W - 1, device=dev, generator=gd).bfloat16(),
+        starts=torch.arange(B + 1, dtype=torch.int32, device=dev), slots=slots.to(torch.int32).to(dev),
+        init=torch.ones(B, dtype=torch.int8, device=dev), y=torch.empty(B, D, device=dev, dtype=torch.bfloat16),
+        T=B, N=B, D=D, W=W, G=G, n_pad=len(pad))
+
+
+def _cumsum(v):
+    s, out = 0, []
+    for a in v:
+        s += a
+        out.append(s)
+    return out
+
+
+def prefill_bytes(b):
+    D, W, T, N, G = b["D"], b["W"], b["T"], b["N"], b["G"]
+    per_token = 2 * D + 2 * W * D // G + 2 * D  # x, w, y
+    return T * per_token + N * 2 * (2 * (W - 1) * D)  # + state read and write
+
+
+def decode_bytes(b):
+    D, W, B, G = b["D"], b["W"], b["T"], b["G"]
+    live = B - b["n_pad"]
+    per_live = 2 * D + 2 * W * D // G + 2 * D + 2 * 2 * (W - 1) * D
+    per_pad = 2 * D + 2 * W * D // G + 2 * D
+    return live * per_live + b["n_pad"] * per_pad
+
+
+def packed_call(vc, b, out=None):
+    return vc.packed_dynamic_conv_triton(b["x"], b["w"], None, b["state"], b["starts"], b["slots"], b["init"],
+                                         b["G"], norm=False, eps=1e-6, out=b["y"] if out is None else out)
+
+
+def time_graph(torch, sets, launch, steps, warmup, dist):
+    """Replay `steps` launches (rotating over `sets`) from one CUDA graph.
+    Returns seconds for the K timed steps (max over ranks)."""
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):
+        for i in range(max(warmup, 3)):
+            launch(sets[i % len(sets)])
+    torch.cuda.current_stream().wait_stream(stream)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for i in range(steps):
+            launch(sets[i % len(sets)])
+    # warm replay (untimed), then the timed replay
+    graph.replay()
+    torch.cuda.synchronize()
+    barrier(dist)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    with torch.cuda.stream(stream):
+        graph.replay()
+    end.record(stream)
+    end.synchronize()
+    torch.cuda.synchronize()
+    barrier(dist)
+    sec = start.elapsed_time(end) / 1e3
+    del graph
+    return reduce_max(torch, dist, sec)
+
+
+def barrier(dist):
+    if dist is not None:
+        dist.barrier()
+
+
+def reduce_max(torch, dist, v):
+    if dist is None:
+        return v
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def n_sets(set_bytes):
+    return max(2, math.ceil(2.5 * L2_BYTES / set_bytes))
+
+
+# ---------------------------------------------------------------------------
+# workload runners
+# ---------------------------------------------------------------------------
+def run_prefill(torch, vc, dev, args, dist, rank, world, peak, traffic):
+    base_seed = 1000 + (rank if args.shard == "requests" else 0)
+    sets = []
+    probe = make_prefill(torch, dev, base_seed, D=args.channels)
+    nbytes = prefill_bytes(probe)
+    for i in range(n_sets(nbytes + probe["state"].numel() * 2)):
+        sets.append(probe if i == 0 else make_prefill(torch, dev, base_seed + 97 * i, D=args.channels))
+    steps = args.steps
+    sec = time_graph(torch, sets, lambda b: packed_call(vc, b), steps, args.warmup, dist)
+    T = probe["T"]
+    per_step = sec / steps
+    achieved = nbytes / per_step / 1e9
+    return dict(tokens_per_step=T, ms_per_step=per_step * 1e3, tokens_per_s=T / per_step, bytes_per_step=nbytes,
+                achieved_gbs=achieved, frac=achieved / peak, sets=len(sets), launches=steps,
+                lengths=probe["lengths"], traffic=traffic.get("prefill"))
+
+
+def run_decode(torch, vc, dev, args, dist, rank, world, peak, traffic):
+    base_seed = 2000 + (rank if args.shard == "requests" else 0)
+    probe = make_decode(torch, dev, base_seed, D=args.channels)
+    nbytes = decode_bytes(probe)
+    set_bytes = nbytes + probe["state"].numel() * 2
+    sets = [probe] + [make_decode(torch, dev, base_seed + 31 * i, D=args.channels) for i in range(1, n_sets(set_bytes))]
+    steps = args.decode_steps
+    sec = time_graph(torch, sets, lambda b: packed_call(vc, b), steps, args.warmup, dist)
+    per_step = sec / steps
+    achieved = nbytes / per_step / 1e9
+    return dict(tokens_per_step=probe["T"], ms_per_step=per_step * 1e3, tokens_per_s=probe["T"] / per_step,
+                bytes_per_step=nbytes, achieved_gbs=achieved, frac=achieved / peak, sets=len(sets), launches=steps,
+                traffic=traffic.get("decode"))
+
+
+def run_train(torch, dev, args, dist, rank, world, peak, traffic):
+    """Training forward + backward through the C ABI (bf16, 8 x 4096 packed)."""
+    from greta_plugin_b200 import _capi
+
+    D, W, G, S, L = args.channels, 4, 1, 8, 4096
+    T = S * L
+    gd = torch.Generator(device=dev).manual_seed(3000 + rank)
+    x = torch.randn(T, D, device=dev, generator=gd).bfloat16()
+    w = (torch.randn(T, W, D // G, device=dev, generator=gd) * 0.5).bfloat16()
+    dout = torch.randn(T, D, device=dev, generator=gd).bfloat16()
+    y, dx, dw = torch.empty_like(x), torch.empty_like(x), torch.empty_like(w)
+    cu = torch.arange(0, T + 1, L, dtype=torch.int32, device=dev)
+    lib = _capi.lib()
+    stream = torch.cuda.current_stream()
+    sp = _capi.stream_of(x)
+    P = _capi.ptr
+
+    def fwd():
+        _capi.check("fwd", lib.greta_dynconv_fwd(_capi.DT_BF16, P(x), P(w), None, P(y), None, P(cu), 0, S, T, D, W, G,
+                                                 0, 1e-6, sp))
+
+    def bwd():
+        _capi.check("bwd", lib.greta_dynconv_bwd(_capi.DT_BF16, P(x), P(w), None, None, P(dout), P(dx), P(dw), None,
+                                                 P(cu), 0, S, T, D, W, G, 0, 1e-6, sp))
+
+    for _ in range(max(args.warmup, 3)):
+        fwd()
+        bwd()
+    torch.cuda.synchronize()
+    barrier(dist)
+    torch.cuda.synchronize()
+    steps = args.train_steps
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3 * steps)]
+    for i in range(steps):
+        ev[3 * i].record(stream)
+        fwd()
+        ev[3 * i + 1].record(stream)
+        bwd()
+        ev[3 * i + 2].record(stream)
+    torch.cuda.synchronize()
+    barrier(dist)
+    f_ms = sum(ev[3 * i].elapsed_time(ev[3 * i + 1]) for i in range(steps)) / steps
+    b_ms = sum(ev[3 * i + 1].elapsed_time(ev[3 * i + 2]) for i in range(steps)) / steps
+    total = ev[0].elapsed_time(ev[-1]) / 1e3
+    total = reduce_max(torch, dist, total)
+    f_ms = reduce_max(torch, dist, f_ms)
+    b_ms = reduce_max(torch, dist, b_ms)
+    fb, bb = T * 12 * D, T * 22 * D
+    return dict(tokens_per_step=T, ms_per_step=total / steps * 1e3, tokens_per_s=T * steps / total,
+                fwd_ms=f_ms, bwd_ms=b_ms, fwd_bytes=fb, bwd_bytes=bb,
+                fwd_gbs=fb / f_ms / 1e6, bwd_gbs=bb / b_ms / 1e6,
+                fwd_frac=fb / f_ms / 1e6 / peak, bwd_frac=bb / b_ms / 1e6 / peak,
+                fwd_tokens_per_s=T / f_ms * 1e3, bwd_tokens_per_s=T / b_ms * 1e3, launches=2 * steps,
+                traffic={"fwd": traffic.get("train_fwd"), "bwd": traffic.get("train_bwd")})
+
+
+def run_e2e_prefill(torch, vc, dev, args, dist):
+    """Public API with host buffers: pinned H2D of the step's inputs, the call,
+    D2H of the output -- all inside the timed region."""
+    b = make_prefill(torch, dev, 4242, D=args.channels)
+    hx = b["x"].cpu().pin_memory()
+    hw = b["w"].cpu().pin_memory()
+    hs = b["starts"].cpu().pin_memory()
+    hsl = b["slots"].cpu().pin_memory()
+    hi = b["init"].cpu().pin_memory()
+    hy = torch.empty(b["y"].shape, dtype=b["y"].dtype).pin_memory()
+    dx, dw = torch.empty_like(b["x"]), torch.empty_like(b["w"])
+    ds, dsl, di = torch.empty_like(b["starts"]), torch.empty_like(b["slots"]), torch.empty_like(b["init"])
+    state = b["state"]
+
+    def step():
+        dx.copy_(hx, non_blocking=True)
+        dw.copy_(hw, non_blocking=True)
+        ds.copy_(hs, non_blocking=True)
+        dsl.copy_(hsl, non_blocking=True)
+        di.copy_(hi, non_blocking=True)
+        y = vc.packed_dynamic_conv_triton(dx, dw, None, state, ds, dsl, di, b["G"], norm=False)
+        hy.copy_(y, non_blocking=True)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    barrier(dist)
+    torch.cuda.synchronize()
+    steps = args.e2e_steps
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(steps):
+        step()
+    e.record()
+    e.synchronize()
+    sec = reduce_max(torch, dist, s.elapsed_time(e) / 1e3)
+    h2d = sum(t.numel() * t.element_size() for t in (hx, hw, hs, hsl, hi))
+    d2h = hy.numel() * hy.element_size()
+    return dict(tokens_per_s=b["T"] * steps / sec, h2d=h2d, d2h=d2h, launches=steps)
+
+
+# ---------------------------------------------------------------------------
+# CPU baselines (the oracle: the reference algorithm restated, host cores)
+# ---------------------------------------------------------------------------
+def cpu_prefill(seconds, threads):
+    import numpy as np
+    import torch
+
+    from oracle import oracle
+
+    b = make_prefill(torch, "cpu", 1000)
+    x, w, st = (b[k].float().numpy() for k in ("x", "w", "state"))
+    starts, slots, init = b["starts"].numpy(), b["slots"].numpy(), b["init"].numpy()
+    oracle.packed(x[:64], w[:64], None, st, [0, 64], slots[:1], init[:1], 1, 0, threads=threads)  # warm
+    n, t0 = 0, time.perf_counter()
+    while True:
+        oracle.packed(x, w, None, st, starts, slots, init, 1, 0, threads=threads)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds or n >= 10000:
+            break
+    del np
+    return dict(value=b["T"] * n / el, unit="tokens/s", cores=threads, kind="port",
+                sample=f"{n} full prefill steps ({b['T']} tokens, C=4096, K=4, fp32 oracle) in {el:.1f} s")
+
+
+def cpu_decode(seconds, threads):
+    import torch
+
+    from oracle import oracle
+
+    b = make_decode(torch, "cpu", 2000)
+    x, w, st = (b[k].float().numpy() for k in ("x", "w", "state"))
+    starts, slots, init = b["starts"].numpy(), b["slots"].numpy(), b["init"].numpy()
+    n, t0 = 0, time.perf_counter()
+    while True:
+        oracle.packed(x, w, None, st, starts, slots, init, 1, 0, threads=threads)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds or n >= 100000:
+            break
+    return dict(value=b["T"] * n / el, unit="tokens/s", cores=threads, kind="port",
+                sample=f"{n} decode steps (256 rows, 1024 slots) in {el:.1f} s")
+
+
+def cpu_train(seconds, threads):
+    """One 4096-token sequence of the training batch, fwd + bwd (bounded sample)."""
+    import numpy as np
+
+    from oracle import oracle
+
+    rng = np.random.default_rng(0)
+    L, D, W = 4096, 4096, 4
+    x = rng.standard_normal((L, D), dtype=np.float32)
+    w = (rng.standard_normal((L, W, D), dtype=np.float32) * 0.5)
+    dy = rng.standard_normal((L, D), dtype=np.float32)
+    n, t0 = 0, time.perf_counter()
+    while True:
+        oracle.fwd(x, w, None, None, 1, 0, threads=threads)
+        oracle.bwd(x, w, None, dy, None, 1, 0, threads=threads)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds or n >= 1000:
+            break
+    return dict(value=L * n / el, unit="tokens/s", cores=threads, kind="port",
+                sample=f"{n} fwd+bwd passes over one 4096-token sequence (of 8) in {el:.1f} s")
+
+
+def host_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+# ---------------------------------------------------------------------------
+def parse():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--workload", choices=["prefill", "decode", "train", "all"], default="all")
+    ap.add_argument("--shard", choices=["requests", "channels"], default="requests")
+    ap.add_argument("--decode-steps", type=int, default=None)
+    ap.add_argument("--train-steps", type=int, default=None)
+    ap.add_argument("--e2e-steps", type=int, default=None)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    a = ap.parse_args()
+    a.decode_steps = a.decode_steps or a.steps
+    a.train_steps = a.train_steps or max(3, min(a.steps, 20))
+    a.e2e_steps = a.e2e_steps or max(3, min(a.steps, 200))
+    return a
+
+
+def config_block(args, world, prefill):
+    par = f"{args.shard} x{world}" if world > 1 else "single GPU"
+    return {"workload": "varlen chunked prefill with cache-slot state (vLLM packed path)",
+            "seqs": 8, "tokens": prefill["tokens_per_step"] if prefill else None,
+            "lengths": prefill.get("lengths") if prefill else None,
+            "channels": args.channels, "kernel_size": 4, "group_size": 1, "norm": False, "gate": False,
+            "state_slots": 64, "l2": f"rotating {prefill['sets'] if prefill else '?'} input sets (> 2x L2)",
+            "parallelism": par}
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    args.channels = 4096 // world if (args.shard == "channels" and world > 1) else 4096
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        threads = host_threads()
+        res = cpu_prefill(min(args.cpu_seconds, 30.0), threads)
+        line = {"metric": METRIC, "value": res["value"], "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": 1e3 * 1 / res["value"] * 1, "higher_is_better": True,
+                "scaling": "weak" if args.shard == "requests" else "strong", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic (seeded N(0,1) inputs in the reference layouts)", "impl": "reference",
+                "config": config_block(args, 1, None),
+                "cpu_baseline": res,
+                "e2e": {"value": res["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        line["ms_per_step"] = None
+        print(json.dumps(line))
+        return
+
+    import torch
+
+    dist = None
+    if world > 1:
+        import torch.distributed as tdist
+        from datetime import timedelta
+
+        torch.cuda.set_device(local)
+        tdist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+        dist = tdist
+    else:
+        torch.cuda.set_device(0)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    from greta_plugin_b200 import vllm_conv as vc
+
+    peak, peak_kind = peaks()
+    traffic = dram_traffic()
+    out = {}
+    with ClockSampler(dev.index) as clocks:
+        if args.workload in ("prefill", "all"):
+            out["prefill"] = run_prefill(torch, vc, dev, args, dist, rank, world, peak, traffic)
+        if args.workload in ("decode", "all"):
+            out["decode"] = run_decode(torch, vc, dev, args, dist, rank, world, peak, traffic)
+        if args.workload in ("train", "all"):
+            out["train"] = run_train(torch, dev, args, dist, rank, world, peak, traffic)
+        e2e = run_e2e_prefill(torch, vc, dev, args, dist) if args.workload in ("prefill", "all") else None
+    clk = clocks.summary()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload in ("prefill", "all"):
+        cpu = cpu_prefill(args.cpu_seconds, host_threads())
+        if args.workload == "all":
+            out.setdefault("decode", {})["cpu_baseline"] = cpu_decode(min(3.0, args.cpu_seconds), host_threads())
+            out.setdefault("train", {})["cpu_baseline"] = cpu_train(min(10.0, args.cpu_seconds), host_threads())
+
+    if dist is not None:
+        dist.barrier()
+    if rank == 0:
+        head = out.get("prefill")
+        launches = sum(v.get("launches", 0) for v in out.values()) + (e2e["launches"] if e2e else 0)
+        if head is None:  # a single non-prefill workload was asked for
+            key = next(iter(out))
+            head = out[key]
+            head.setdefault("achieved_gbs", head.get("bwd_gbs"))
+            head.setdefault("frac", head.get("bwd_frac"))
+        scale = world if args.shard == "requests" else 1
+        line = {
+            "metric": METRIC,
+            "value": head["tokens_per_s"] * scale,
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": head["ms_per_step"],
+            "higher_is_better": True,
+            "scaling": "weak" if args.shard == "requests" else "strong",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) inputs in the reference layouts)",
+            "config": config_block(args, world, out.get("prefill")),
+            "roofline": {"bound": "hbm", "achieved": head["achieved_gbs"], "peak": peak, "unit": "GB/s",
+                         "frac": head["frac"], "traffic": head.get("traffic"),
+                         "peak_source": f"{peak_kind} copy bandwidth (MEASURED_PEAKS.json hbm_gbs)"
+                         if peak_kind == "measured" else "fallback 6.65 TB/s",
+                         "frac_of_8tbs_spec": head["achieved_gbs"] / 8000.0},
+            "cpu_baseline": cpu,
+            "e2e": None if e2e is None else {"value": e2e["tokens_per_s"] * scale, "unit": "tokens/s",
+                                             "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"]},
+            "gpu_launches": launches,
+            "clocks": clk,
+            "workloads": out,
+        }
+        print(json.dumps(line))
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -97,8 +97,9 @@ int greta_dynconv_fwd(int dtype, const void* x, const void* w, const void* gate,
                       int64_t D, int64_t W, int64_t G, int norm, float eps, void* stream) {
   int rc = check_common(dtype, D, W, G, norm);
   if (rc) return rc;
-  if (!x || !w || !y || T < 0 || (cu_seqlens && num_seqs < 0)) return GRETA_ERR_INVALID_ARG;
-  if (T == 0 || (cu_seqlens && num_seqs == 0)) return GRETA_OK;
+  if (T < 0 || (cu_seqlens && num_seqs < 0)) return GRETA_ERR_INVALID_ARG;
+  if (T == 0 || (cu_seqlens && num_seqs == 0)) return GRETA_OK;  // empty tensors may have null pointers
+  if (!x || !w || !y) return GRETA_ERR_INVALID_ARG;
   const int nv = pick_nv(dtype, D, G, {x, gate, y, yr}, w);
   if (nv == 0) return GRETA_ERR_ALIGNMENT;
   const int H = (int)W - 1;
@@ -124,10 +125,11 @@ int greta_dynconv_bwd(int dtype, const void* x, const void* w, const void* gate,
   int rc = check_common(dtype, D, W, G, norm);
   if (rc) return rc;
   if (norm == GRETA_NORM_STABLE) return GRETA_ERR_UNSUPPORTED;
-  if (!x || !w || !dout || !dx || !dw || T < 0 || (cu_seqlens && num_seqs < 0)) return GRETA_ERR_INVALID_ARG;
+  if (T < 0 || (cu_seqlens && num_seqs < 0)) return GRETA_ERR_INVALID_ARG;
+  if (T == 0 || (cu_seqlens && num_seqs == 0)) return GRETA_OK;  // empty tensors may have null pointers
+  if (!x || !w || !dout || !dx || !dw) return GRETA_ERR_INVALID_ARG;
   if ((gate == nullptr) != (dg == nullptr)) return GRETA_ERR_INVALID_ARG;
   if (norm != GRETA_NORM_NONE && yr == nullptr) return GRETA_ERR_INVALID_ARG;
-  if (T == 0 || (cu_seqlens && num_seqs == 0)) return GRETA_OK;
   int nv = pick_nv(dtype, D, G, {x, gate, yr, dout, dx, dg}, w);
   if (nv == kVec && !aligned(dw, (int64_t)group_vec(kVec, G) * esize(dtype))) nv = G > 32 ? 0 : 1;
   if (nv == 0) return GRETA_ERR_ALIGNMENT;
@@ -153,8 +155,9 @@ int greta_dynconv_inference(int dtype, const void* context, const void* w, const
                             void* stream) {
   int rc = check_common(dtype, D, W, G, norm);
   if (rc) return rc;
-  if (!context || !w || !y || B < 0 || Q < 0) return GRETA_ERR_INVALID_ARG;
-  if (B == 0 || Q == 0) return GRETA_OK;
+  if (B < 0 || Q < 0) return GRETA_ERR_INVALID_ARG;
+  if (B == 0 || Q == 0) return GRETA_OK;  // empty tensors may have null pointers
+  if (!context || !w || !y) return GRETA_ERR_INVALID_ARG;
   const int nv = pick_nv(dtype, D, G, {context, gate, y}, w);
   if (nv == 0) return GRETA_ERR_ALIGNMENT;
   const int H = (int)W - 1;
@@ -177,8 +180,9 @@ int greta_dynconv_decode_rows(int dtype, const void* x, const void* w, const voi
                               void* stream) {
   int rc = check_common(dtype, D, W, G, norm);
   if (rc) return rc;
-  if (!x || !w || !conv_state || !y || B < 0 || W < 2) return GRETA_ERR_INVALID_ARG;
-  if (B == 0) return GRETA_OK;
+  if (B < 0 || W < 2) return GRETA_ERR_INVALID_ARG;
+  if (B == 0) return GRETA_OK;  // empty tensors may have null pointers
+  if (!x || !w || !conv_state || !y) return GRETA_ERR_INVALID_ARG;
   if (B > INT_MAX) return GRETA_ERR_INVALID_ARG;
   const int nv = pick_nv(dtype, D, G, {x, gate, y}, w);
   if (nv == 0) return GRETA_ERR_ALIGNMENT;
@@ -205,10 +209,10 @@ int greta_dynconv_packed_state(int dtype, const void* x, const void* w, const vo
   int rc = check_common(dtype, D, W, G, norm);
   if (rc) return rc;
   const int H = (int)W - 1;
-  if (!x || !w || !y || !starts || !slots || !has_initial || T < 0 || num_reqs < 0 || num_slots < 0)
-    return GRETA_ERR_INVALID_ARG;
+  if (T < 0 || num_reqs < 0 || num_slots < 0) return GRETA_ERR_INVALID_ARG;
+  if (T == 0 || num_reqs == 0) return GRETA_OK;  // empty tensors may have null pointers
+  if (!x || !w || !y || !starts || !slots || !has_initial) return GRETA_ERR_INVALID_ARG;
   if (H > 0 && !state && num_slots > 0) return GRETA_ERR_INVALID_ARG;
-  if (T == 0 || num_reqs == 0) return GRETA_OK;
   const int nv = pick_nv(dtype, D, G, {x, gate, y}, w);
   if (nv == 0) return GRETA_ERR_ALIGNMENT;
   const int es = esize(dtype);

@@ -129,11 +129,16 @@ void oracle_fwd(const float* x, const float* w, const float* gate, const int64_t
 
 /*
  * Training backward: dx [T, D], dw [T, W, D/G], dg [T, D] (dg only with gate).
- * norm 0 or 1 (plain), as in the reference training path.
+ * norm 0 or 1 (plain), as in the reference training path. With norm, `yr`
+ * (may be NULL) is the pre-norm output saved by the forward, in the I/O
+ * precision: the reference backward kernel reads it from memory
+ * (greta/dynamic_conv.py:328-342) instead of recomputing it, and with 16-bit
+ * I/O its rounding matters for groups whose RMS is tiny. NULL recomputes it
+ * exactly (the autograd-through-torch form, :937-962).
  */
-void oracle_bwd(const float* x, const float* w, const float* gate, const float* dout, const int64_t* cu,
-                int64_t nseq, int64_t T, int64_t D, int64_t W, int64_t G, int norm, double eps, float* dx,
-                float* dw, float* dg, int threads) {
+void oracle_bwd(const float* x, const float* w, const float* gate, const float* dout, const float* yr,
+                const int64_t* cu, int64_t nseq, int64_t T, int64_t D, int64_t W, int64_t G, int norm, double eps,
+                float* dx, float* dw, float* dg, int threads) {
   set_threads(threads);
   const int64_t H = W - 1, DC = D / G;
   int64_t one[2] = {0, T};
@@ -159,11 +164,15 @@ void oracle_bwd(const float* x, const float* w, const float* gate, const float* 
         continue;
       }
       const int64_t a = starts[seq[t]];
-      for (int64_t d = 0; d < D; ++d) acc[d] = 0;
-      for (int64_t k = 0; k < W; ++k) {
-        const int64_t src = t + k - H;
-        if (src < a) continue;
-        for (int64_t d = 0; d < D; ++d) acc[d] += (double)x[src * D + d] * (double)w[(t * W + k) * DC + d / G];
+      if (norm && yr) {
+        for (int64_t d = 0; d < D; ++d) acc[d] = yr[t * D + d];
+      } else {
+        for (int64_t d = 0; d < D; ++d) acc[d] = 0;
+        for (int64_t k = 0; k < W; ++k) {
+          const int64_t src = t + k - H;
+          if (src < a) continue;
+          for (int64_t d = 0; d < D; ++d) acc[d] += (double)x[src * D + d] * (double)w[(t * W + k) * DC + d / G];
+        }
       }
       for (int64_t d = 0; d < D; ++d) {
         const double o = dout[t * D + d];

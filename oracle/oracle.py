@@ -53,7 +53,8 @@ def _load():
     P = ctypes.c_void_p
     I = ctypes.c_int64
     lib.oracle_fwd.argtypes = [P, P, P, P, I, I, I, I, I, ctypes.c_int, ctypes.c_double, P, P, ctypes.c_int]
-    lib.oracle_bwd.argtypes = [P, P, P, P, P, I, I, I, I, I, ctypes.c_int, ctypes.c_double, P, P, P, ctypes.c_int]
+    lib.oracle_bwd.argtypes = [P, P, P, P, P, P, I, I, I, I, I, ctypes.c_int, ctypes.c_double, P, P, P,
+                               ctypes.c_int]
     lib.oracle_inference.argtypes = [P, P, P, I, I, I, I, I, ctypes.c_int, ctypes.c_double, P, ctypes.c_int]
     lib.oracle_decode_rows.argtypes = [P, P, P, P, I, I, I, I, ctypes.c_int, ctypes.c_double, P, ctypes.c_int]
     lib.oracle_packed.argtypes = [P, P, P, P, I, I, I, I, P, P, P, I, I, I, I, I, ctypes.c_int, ctypes.c_double,
@@ -98,17 +99,20 @@ def fwd(x, w, gate, cu_seqlens, group_size, norm=NORM_NONE, eps=1e-6, save_pre=F
     return y, yr
 
 
-def bwd(x, w, gate, dout, cu_seqlens, group_size, norm=NORM_NONE, eps=1e-6, threads=0):
-    """Returns (dx [T, D], dw [T, W, D/G], dg [T, D] or None)."""
-    x, w, gate, dout, cu = _f32(x), _f32(w), _f32(gate), _f32(dout), _i64(cu_seqlens)
+def bwd(x, w, gate, dout, cu_seqlens, group_size, norm=NORM_NONE, eps=1e-6, yr=None, threads=0):
+    """Returns (dx [T, D], dw [T, W, D/G], dg [T, D] or None).
+
+    yr: the pre-norm output as saved by the forward (I/O precision), which the
+    reference backward kernel reads; None recomputes it in double precision."""
+    x, w, gate, dout, cu, yr = _f32(x), _f32(w), _f32(gate), _f32(dout), _i64(cu_seqlens), _f32(yr)
     T, D = x.shape
     W = w.shape[1]
     dx = np.zeros((T, D), np.float32)
     dw = np.zeros(w.shape, np.float32)
     dg = np.zeros((T, D), np.float32) if gate is not None else None
     nseq = 0 if cu is None else cu.shape[0] - 1
-    _load().oracle_bwd(_p(x), _p(w), _p(gate), _p(dout), _p(cu), nseq, T, D, W, group_size, norm, eps, _p(dx),
-                       _p(dw), _p(dg), threads)
+    _load().oracle_bwd(_p(x), _p(w), _p(gate), _p(dout), _p(yr), _p(cu), nseq, T, D, W, group_size, norm, eps,
+                       _p(dx), _p(dw), _p(dg), threads)
     return dx, dw, dg
 
 

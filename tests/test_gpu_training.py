@@ -13,7 +13,12 @@ pytestmark = pytest.mark.gpu
 
 
 def run_case(T_lens, D, W, G, norm, gate_on, dtype, seed=0, cu_dtype=torch.int32, use_cu=True):
+    """Forward (saving the pre-norm output) and backward through the drop-in
+    layer, compared with the oracle. The oracle backward reads the same saved
+    pre-norm output as the kernel, as the reference backward kernel does. The
+    autograd path must reproduce the explicit calls bit for bit."""
     from greta_plugin_b200 import dynamic_causal_conv1d
+    from greta_plugin_b200.dynamic_conv import dynconv_bwd, dynconv_fwd
 
     g = torch.Generator().manual_seed(seed)
     T = int(sum(T_lens))
@@ -22,21 +27,34 @@ def run_case(T_lens, D, W, G, norm, gate_on, dtype, seed=0, cu_dtype=torch.int32
     gate = rand(g, 1, T, D, dtype=dtype) if gate_on else None
     dout = rand(g, 1, T, D, dtype=dtype)
     cu = ragged_cu(T_lens).to(cu_dtype) if use_cu else None
-    xd = x.to(DEV).requires_grad_()
-    wd = w.to(DEV).requires_grad_()
-    gd = gate.to(DEV).requires_grad_() if gate_on else None
-    y = dynamic_causal_conv1d(xd, wd, gd, cu.to(DEV) if use_cu else None, G, norm, 1e-6)
-    y.backward(dout.to(DEV))
+    xd, wd, dd = x.to(DEV), w.to(DEV), dout.to(DEV)
+    gd = gate.to(DEV) if gate_on else None
+    cud = cu.to(DEV) if use_cu else None
+    y, yr, BT, ci = dynconv_fwd(xd, wd, gd, cud, G, norm=norm, eps=1e-6, save_pre=True)
+    dx, dw, dg = dynconv_bwd(xd, wd, gd, yr, dd, cud, G, norm, 1e-6, BT, ci)
+    assert y.dtype == dtype and dw.dtype == dtype
+
     cu_np = cu.numpy() if use_cu else None
-    yo, _ = oracle.fwd(to_np(x[0]), to_np(w), to_np(gate[0]) if gate_on else None, cu_np, G, int(norm))
-    dxo, dwo, dgo = oracle.bwd(to_np(x[0]), to_np(w), to_np(gate[0]) if gate_on else None, to_np(dout[0]), cu_np,
-                               G, int(norm))
-    assert y.dtype == dtype and wd.grad.dtype == dtype
+    gn = to_np(gate[0]) if gate_on else None
+    yo, yro = oracle.fwd(to_np(x[0]), to_np(w), gn, cu_np, G, int(norm), save_pre=True)
     assert_close(y[0], yo, dtype)
-    assert_close(xd.grad[0], dxo, dtype)
-    assert_close(wd.grad, dwo, dtype)
+    if norm:
+        assert_close(yr[0], yro, dtype)
+    dxo, dwo, dgo = oracle.bwd(to_np(x[0]), to_np(w), gn, to_np(dout[0]), cu_np, G, int(norm),
+                               yr=to_np(yr[0]) if norm else None)
+    assert_close(dx[0], dxo, dtype)
+    assert_close(dw, dwo, dtype)
     if gate_on:
-        assert_close(gd.grad[0], dgo, dtype)
+        assert_close(dg[0], dgo, dtype)
+
+    xa, wa = xd.clone().requires_grad_(), wd.clone().requires_grad_()
+    ga = gd.clone().requires_grad_() if gate_on else None
+    ya = dynamic_causal_conv1d(xa, wa, ga, cud, G, norm, 1e-6)
+    ya.backward(dd)
+    assert torch.equal(ya, y)
+    assert torch.equal(xa.grad, dx) and torch.equal(wa.grad, dw)
+    if gate_on:
+        assert torch.equal(ga.grad, dg)
 
 
 @pytest.mark.parametrize("G", [1, 2, 4, 8, 16, 32, 64, 128])
