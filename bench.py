@@ -275,7 +275,7 @@ def run_train(torch, dev, args, dist, rank, world, peak, traffic):
     """Training forward + backward through the C ABI (bf16, 8 x 4096 packed)."""
     from greta_plugin_b200 import _capi
 
-    D, W, G, S, L = args.channels, 4, 1, 8, 4096
+    D, W, G, S, L = args.channels, 4, 1, args.train_seqs, 4096
     T = S * L
     gd = torch.Generator(device=dev).manual_seed(3000 + rank)
     x = torch.randn(T, D, device=dev, generator=gd).bfloat16()
@@ -456,7 +456,12 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ncu", action="store_true",
+                    help="profiling mode: plain launches (no CUDA graph), no e2e or CPU arm, no JSON line")
+    ap.add_argument("--train-seqs", type=int, default=8,
+                    help="4096-token sequences in the training batch (8 = the full configuration)")
     a = ap.parse_args()
+    a.channels = 4096
     a.decode_steps = a.decode_steps or a.steps
     a.train_steps = a.train_steps or max(3, min(a.steps, 20))
     a.e2e_steps = a.e2e_steps or max(3, min(a.steps, 200))
@@ -473,8 +478,48 @@ def config_block(args, world, prefill):
             "parallelism": par}
 
 
+def profile_launches(args):
+    """--ncu: each selected workload's kernels launched `steps` times after
+    `warmup` launches, on plain streams, so that ncu sees ordinary launches."""
+    import torch
+
+    from greta_plugin_b200 import _capi
+    from greta_plugin_b200 import vllm_conv as vc
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    n = args.warmup + args.steps
+    if args.workload in ("prefill", "all"):
+        b = make_prefill(torch, dev, 1000, D=args.channels)
+        for _ in range(n):
+            packed_call(vc, b)
+    if args.workload in ("decode", "all"):
+        b = make_decode(torch, dev, 2000, D=args.channels)
+        for _ in range(n):
+            packed_call(vc, b)
+    if args.workload in ("train", "all"):
+        D, W, G, L = args.channels, 4, 1, 4096
+        T = args.train_seqs * L
+        gd = torch.Generator(device=dev).manual_seed(3000)
+        x = torch.randn(T, D, device=dev, generator=gd).bfloat16()
+        w = (torch.randn(T, W, D, device=dev, generator=gd) * 0.5).bfloat16()
+        dout = torch.randn(T, D, device=dev, generator=gd).bfloat16()
+        y, dx, dw = torch.empty_like(x), torch.empty_like(x), torch.empty_like(w)
+        cu = torch.arange(0, T + 1, L, dtype=torch.int32, device=dev)
+        lib, P, sp = _capi.lib(), _capi.ptr, _capi.stream_of(x)
+        for _ in range(n):
+            _capi.check("fwd", lib.greta_dynconv_fwd(_capi.DT_BF16, P(x), P(w), None, P(y), None, P(cu), 0,
+                                                     args.train_seqs, T, D, W, G, 0, 1e-6, sp))
+            _capi.check("bwd", lib.greta_dynconv_bwd(_capi.DT_BF16, P(x), P(w), None, None, P(dout), P(dx), P(dw),
+                                                     None, P(cu), 0, args.train_seqs, T, D, W, G, 0, 1e-6, sp))
+    torch.cuda.synchronize()
+
+
 def main():
     args = parse()
+    if args.ncu:
+        profile_launches(args)
+        return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))

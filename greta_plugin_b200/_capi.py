@@ -48,10 +48,11 @@ def lib() -> ctypes.CDLL:
     L.greta_dynconv_packed_state.argtypes = [I32, P, P, P, P, P, I64, I64, I64, I64, P, P, P, I64, I64, I64, I64,
                                              I64, I32, F, P, P]
     L.greta_dynconv_supports.argtypes = [I64, I64]
+    L.greta_dynconv_set_launch_shape.argtypes = [I32, I32, I32, I32]
     L.greta_dynconv_status_string.argtypes = [I32]
     L.greta_dynconv_status_string.restype = ctypes.c_char_p
     L.greta_dynconv_version.restype = I32
-    for name in ("fwd", "bwd", "inference", "decode_rows", "packed_state", "supports"):
+    for name in ("fwd", "bwd", "inference", "decode_rows", "packed_state", "supports", "set_launch_shape"):
         getattr(L, f"greta_dynconv_{name}").restype = I32
     _lib = L
     return L
@@ -78,6 +79,14 @@ def check(fn: str, status: int) -> None:
         if status in (ERR_INVALID_ARG, ERR_UNSUPPORTED, ERR_ALIGNMENT):
             raise ValueError(f"{fn}: {msg}")
         raise GretaKernelError(fn, status, msg)
+
+
+PATH_FWD, PATH_BWD, PATH_INFERENCE, PATH_DECODE_ROWS, PATH_PACKED_PREFILL, PATH_PACKED_DECODE = range(6)
+
+
+def set_launch_shape(path: int, block_x: int = 0, block_y: int = 0, tokens: int = 0) -> None:
+    """Override (or, with zeros, restore) the CTA shape of one launch path."""
+    check("greta_dynconv_set_launch_shape", lib().greta_dynconv_set_launch_shape(path, block_x, block_y, tokens))
 
 
 def version() -> int:

@@ -20,7 +20,7 @@
 namespace greta {
 
 __device__ __forceinline__ bool resolve_bwd_chunk(const BwdParams& p, ChunkInfo& ci) {
-  const long long cid = blockIdx.x;
+  const long long cid = blockIdx.x / p.nblk;
   ci.slot = -1;
   ci.has_state = 0;
   ci.hist = kHistZero;
@@ -61,7 +61,7 @@ __global__ void __launch_bounds__(256) dynconv_bwd_kernel(const BwdParams p) {
   ChunkInfo ci;
   if (!resolve_bwd_chunk(p, ci)) return;
 
-  const int d0 = (blockIdx.y * blockDim.x + threadIdx.x) * NV;
+  const int d0 = ((int)(blockIdx.x % p.nblk) * blockDim.x + threadIdx.x) * NV;
   const bool active = d0 < D;
   const int lpg = (GV == 1 && G > NV) ? G / NV : 1;
   const bool dw_writer = active && (GV > 1 || (threadIdx.x & (lpg - 1)) == 0);

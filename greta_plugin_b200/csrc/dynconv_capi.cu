@@ -54,13 +54,15 @@ int pick_nv(int dtype, int64_t D, int64_t G, std::initializer_list<const void*> 
   return 1;
 }
 
+// 1-D grid of chunks x channel blocks, channel block fastest.
 LaunchShape make_shape(long long chunks, int64_t D, int nv, int tx, int ty) {
   const long long lanes = (D + nv - 1) / nv;
   const long long need = ((lanes + 31) / 32) * 32;
   if (tx > need) tx = (int)need;
   LaunchShape s;
   s.block = dim3(tx, ty, 1);
-  s.grid = dim3((unsigned)chunks, (unsigned)((lanes + tx - 1) / tx), 1);
+  s.nblk = (int)((lanes + tx - 1) / tx);
+  s.grid = dim3((unsigned)(chunks * s.nblk), 1, 1);
   return s;
 }
 
@@ -88,6 +90,35 @@ cudaError_t run_bwd(int dtype, const BwdParams& p, int nv, int norm, const Launc
 
 long long cdiv(long long a, long long b) { return (a + b - 1) / b; }
 
+// Built-in CTA shapes per launch path: {threads along channels (tx), token
+// runs per CTA (ty), tokens per run (L)}; a CTA owns tx*8 channels of ty*L
+// consecutive tokens and each thread walks one run. Long streams use 32x4
+// CTAs; the backward uses longer runs to amortise its W-1 row right halo;
+// packed prefill uses short runs so a ~1k-token batch spreads over the GPU;
+// decode has one token per request and uses wide CTAs.
+struct Shape {
+  int tx, ty, L;
+};
+constexpr int kPaths = 6;
+constexpr Shape kDefaultShape[kPaths] = {
+    {32, 4, 16},   // GRETA_PATH_FWD
+    {32, 4, 32},   // GRETA_PATH_BWD
+    {32, 4, 16},   // GRETA_PATH_INFERENCE
+    {256, 1, 1},   // GRETA_PATH_DECODE_ROWS
+    {32, 2, 8},    // GRETA_PATH_PACKED_PREFILL
+    {128, 1, 16},  // GRETA_PATH_PACKED_DECODE
+};
+Shape g_override[kPaths] = {};
+
+// A run must cover the W-1 history positions: a request's old slot taps are
+// then only read by row 0 of its first chunk.
+Shape shape_for(int path, int H) {
+  Shape s = g_override[path].tx > 0 ? g_override[path] : kDefaultShape[path];
+  if (s.L < H) s.L = H;
+  if (s.L < 1) s.L = 1;
+  return s;
+}
+
 }  // namespace
 
 extern "C" {
@@ -102,20 +133,18 @@ int greta_dynconv_fwd(int dtype, const void* x, const void* w, const void* gate,
   if (!x || !w || !y) return GRETA_ERR_INVALID_ARG;
   const int nv = pick_nv(dtype, D, G, {x, gate, y, yr}, w);
   if (nv == 0) return GRETA_ERR_ALIGNMENT;
-  const int H = (int)W - 1;
-  const int ty = 4;
-  const int L = H > 16 ? H : 16;
+  const Shape sh = shape_for(GRETA_PATH_FWD, (int)W - 1);
   FwdParams p{};
   p.x = x; p.w = w; p.g = gate; p.y = y; p.yr = norm != GRETA_NORM_NONE ? yr : nullptr;
   p.starts = cu_seqlens; p.starts_i64 = cu_seqlens_int64 ? 1 : 0;
   p.mode = cu_seqlens ? kModePacked : kModeSingle;
   p.nseq = cu_seqlens ? num_seqs : 1;
   p.T = T; p.D = (int)D; p.W = (int)W; p.G = (int)G;
-  p.L = L; p.chunk = L * ty;
+  p.L = sh.L; p.chunk = sh.L * sh.ty;
   p.eps = eps;
   const long long chunks = cdiv(T, p.chunk) + (cu_seqlens ? num_seqs : 0);
-  if (chunks > INT_MAX) return GRETA_ERR_INVALID_ARG;
-  return finish(run_fwd(dtype, p, nv, norm, make_shape(chunks, D, nv, 32, ty), stream));
+  if (chunks * (D / 8 + 1) > INT_MAX) return GRETA_ERR_INVALID_ARG;
+  return finish(run_fwd(dtype, p, nv, norm, make_shape(chunks, D, nv, sh.tx, sh.ty), stream));
 }
 
 int greta_dynconv_bwd(int dtype, const void* x, const void* w, const void* gate, const void* yr,
@@ -133,9 +162,7 @@ int greta_dynconv_bwd(int dtype, const void* x, const void* w, const void* gate,
   int nv = pick_nv(dtype, D, G, {x, gate, yr, dout, dx, dg}, w);
   if (nv == kVec && !aligned(dw, (int64_t)group_vec(kVec, G) * esize(dtype))) nv = G > 32 ? 0 : 1;
   if (nv == 0) return GRETA_ERR_ALIGNMENT;
-  const int H = (int)W - 1;
-  const int ty = 4;
-  const int L = H > 32 ? H : 32;
+  const Shape sh = shape_for(GRETA_PATH_BWD, (int)W - 1);
   BwdParams p{};
   p.x = x; p.w = w; p.g = gate; p.yr = norm != GRETA_NORM_NONE ? yr : nullptr; p.dout = dout;
   p.dx = dx; p.dw = dw; p.dg = dg;
@@ -143,11 +170,11 @@ int greta_dynconv_bwd(int dtype, const void* x, const void* w, const void* gate,
   p.mode = cu_seqlens ? kModePacked : kModeSingle;
   p.nseq = cu_seqlens ? num_seqs : 1;
   p.T = T; p.D = (int)D; p.W = (int)W; p.G = (int)G;
-  p.L = L; p.chunk = L * ty;
+  p.L = sh.L; p.chunk = sh.L * sh.ty;
   p.eps = eps;
   const long long chunks = cdiv(T, p.chunk) + (cu_seqlens ? num_seqs : 0);
-  if (chunks > INT_MAX) return GRETA_ERR_INVALID_ARG;
-  return finish(run_bwd(dtype, p, nv, norm, make_shape(chunks, D, nv, 32, ty), stream));
+  if (chunks * (D / 8 + 1) > INT_MAX) return GRETA_ERR_INVALID_ARG;
+  return finish(run_bwd(dtype, p, nv, norm, make_shape(chunks, D, nv, sh.tx, sh.ty), stream));
 }
 
 int greta_dynconv_inference(int dtype, const void* context, const void* w, const void* gate, void* y,
@@ -160,19 +187,17 @@ int greta_dynconv_inference(int dtype, const void* context, const void* w, const
   if (!context || !w || !y) return GRETA_ERR_INVALID_ARG;
   const int nv = pick_nv(dtype, D, G, {context, gate, y}, w);
   if (nv == 0) return GRETA_ERR_ALIGNMENT;
-  const int H = (int)W - 1;
-  const int ty = 4;
-  const int L = H > 16 ? H : 16;
+  const Shape sh = shape_for(GRETA_PATH_INFERENCE, (int)W - 1);
   FwdParams p{};
   p.x = context; p.w = w; p.g = gate; p.y = y; p.yr = nullptr;
   p.mode = kModeContext;
   p.nseq = B;
   p.T = Q; p.D = (int)D; p.W = (int)W; p.G = (int)G;
-  p.L = L; p.chunk = L * ty;
+  p.L = sh.L; p.chunk = sh.L * sh.ty;
   p.eps = eps;
   const long long chunks = B * cdiv(Q, p.chunk);
-  if (chunks > INT_MAX) return GRETA_ERR_INVALID_ARG;
-  return finish(run_fwd(dtype, p, nv, norm, make_shape(chunks, D, nv, 32, ty), stream));
+  if (chunks * (D / 8 + 1) > INT_MAX) return GRETA_ERR_INVALID_ARG;
+  return finish(run_fwd(dtype, p, nv, norm, make_shape(chunks, D, nv, sh.tx, sh.ty), stream));
 }
 
 int greta_dynconv_decode_rows(int dtype, const void* x, const void* w, const void* gate, void* conv_state,
@@ -193,12 +218,13 @@ int greta_dynconv_decode_rows(int dtype, const void* x, const void* w, const voi
   p.mode = kModeRows;
   p.nseq = B;
   p.T = B; p.D = (int)D; p.W = (int)W; p.G = (int)G;
-  p.L = H; p.chunk = H;
+  p.L = 1; p.chunk = 1;  // one token per request
   p.state = conv_state;
   p.s_slot = D * H; p.s_d = H; p.s_h = 1; p.num_slots = B;
   p.st_layout = (nv == kVec && aligned(conv_state, (int64_t)kVec * es)) ? kStDS : kStGeneric;
   p.eps = eps;
-  return finish(run_fwd(dtype, p, nv, norm, make_shape(B, D, nv, 128, 1), stream));
+  const Shape sh = shape_for(GRETA_PATH_DECODE_ROWS, H);
+  return finish(run_fwd(dtype, p, nv, norm, make_shape(B, D, nv, sh.tx, 1), stream));
 }
 
 int greta_dynconv_packed_state(int dtype, const void* x, const void* w, const void* gate, void* y,
@@ -217,16 +243,14 @@ int greta_dynconv_packed_state(int dtype, const void* x, const void* w, const vo
   if (nv == 0) return GRETA_ERR_ALIGNMENT;
   const int es = esize(dtype);
   const bool decode_like = T <= 2 * num_reqs;
-  const int ty = decode_like ? 1 : 4;
-  int L = decode_like ? 4 : 8;
-  if (L < H) L = H;
+  const Shape sh = shape_for(decode_like ? GRETA_PATH_PACKED_DECODE : GRETA_PATH_PACKED_PREFILL, H);
   FwdParams p{};
   p.x = x; p.w = w; p.g = gate; p.y = y; p.yr = nullptr;
   p.starts = starts; p.starts_i64 = 0;
   p.mode = kModePacked;
   p.nseq = num_reqs;
   p.T = T; p.D = (int)D; p.W = (int)W; p.G = (int)G;
-  p.L = L; p.chunk = L * ty;
+  p.L = sh.L; p.chunk = sh.L * sh.ty;
   p.slots = slots;
   p.initial = reinterpret_cast<const signed char*>(has_initial);
   p.err = error_flags;
@@ -248,8 +272,20 @@ int greta_dynconv_packed_state(int dtype, const void* x, const void* w, const vo
     p.num_slots = 0;
   }
   const long long chunks = cdiv(T, p.chunk) + num_reqs;
-  if (chunks > INT_MAX) return GRETA_ERR_INVALID_ARG;
-  return finish(run_fwd(dtype, p, nv, norm, make_shape(chunks, D, nv, decode_like ? 128 : 32, ty), stream));
+  if (chunks * (D / 8 + 1) > INT_MAX) return GRETA_ERR_INVALID_ARG;
+  return finish(run_fwd(dtype, p, nv, norm, make_shape(chunks, D, nv, sh.tx, sh.ty), stream));
+}
+
+int greta_dynconv_set_launch_shape(int path, int block_x, int block_y, int tokens) {
+  if (path < 0 || path >= kPaths) return GRETA_ERR_INVALID_ARG;
+  if (block_x <= 0 || block_y <= 0 || tokens <= 0) {
+    g_override[path] = Shape{0, 0, 0};
+    return GRETA_OK;
+  }
+  if (block_x % 32 != 0 || block_x * block_y > 256) return GRETA_ERR_INVALID_ARG;
+  if (path == GRETA_PATH_DECODE_ROWS && block_y != 1) return GRETA_ERR_INVALID_ARG;
+  g_override[path] = Shape{block_x, block_y, tokens};
+  return GRETA_OK;
 }
 
 int greta_dynconv_supports(int64_t group_size, int64_t channels) {

@@ -1,9 +1,10 @@
 // Shared device code for the dynamic causal depthwise convolution kernels.
 //
 // Work decomposition (all kernels):
-//   grid.x  = chunks: a chunk is a run of consecutive tokens of ONE sequence
-//             (sequence = packed request, cu_seqlens segment, batch row).
-//   grid.y  = channel blocks of blockDim.x * NV channels.
+//   grid.x  = chunks x channel blocks, channel block fastest: a chunk is a
+//             run of consecutive tokens of ONE sequence (sequence = packed
+//             request, cu_seqlens segment, batch row); a channel block is
+//             blockDim.x * NV channels.
 //   thread  = NV consecutive channels (one 16-byte vector for 16-bit types)
 //             x a run of L consecutive tokens; threadIdx.y picks the run
 //             inside the chunk. A thread walks its run in time order and
@@ -46,6 +47,7 @@ struct FwdParams {
   int D, W, G;
   int L;               // tokens per thread run
   int chunk;           // tokens per CTA = L * blockDim.y
+  int nblk;            // channel blocks; blockIdx.x = chunk * nblk + channel block
   // cache-slot state
   void* state;         // null = no state
   long long s_slot, s_d, s_h, num_slots;
@@ -73,6 +75,7 @@ struct BwdParams {
   int D, W, G;
   int L;
   int chunk;
+  int nblk;  // channel blocks; blockIdx.x = chunk * nblk + channel block
   float eps;
 };
 
@@ -314,3 +317,62 @@ __device__ bool block_find_chunk(const void* starts, int is64, long long nseq, l
 
 }  // namespace greta
 
+
+namespace greta {
+
+// ---------------------------------------------------------------------------
+// per-thread asynchronous global->shared copies (cp.async). A thread stages
+// its own operands in shared memory; only the thread that issued a copy reads
+// it (after cp.async.wait_group), so no barrier is involved. With pred false
+// nothing is read and the destination is zero-filled.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ unsigned smem_addr(const void* p) {
+  return static_cast<unsigned>(__cvta_generic_to_shared(p));
+}
+
+template <int BYTES>
+__device__ __forceinline__ void cp_async(void* dst, const void* src, bool pred) {
+  static_assert(BYTES == 4 || BYTES == 8 || BYTES == 16, "cp.async moves 4, 8 or 16 bytes");
+  const unsigned n = pred ? BYTES : 0;
+  if constexpr (BYTES == 16) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(smem_addr(dst)), "l"(src), "r"(n)
+                 : "memory");
+  } else {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], %2, %3;\n" ::"r"(smem_addr(dst)), "l"(src), "n"(BYTES),
+                 "r"(n)
+                 : "memory");
+  }
+}
+
+// Copy one pack of BYTES (a multiple of 16, or 4 / 8). Smaller packs are
+// never staged (callers keep them in registers); the empty branch only lets
+// such instantiations compile.
+template <int BYTES>
+__device__ __forceinline__ void cp_async_pack(void* dst, const void* src, bool pred) {
+  if constexpr (BYTES >= 16) {
+#pragma unroll
+    for (int o = 0; o < BYTES; o += 16)
+      cp_async<16>(static_cast<char*>(dst) + o, static_cast<const char*>(src) + o, pred);
+  } else if constexpr (BYTES == 4 || BYTES == 8) {
+    cp_async<BYTES>(dst, src, pred);
+  }
+}
+
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+// wait until at most `pending` (runtime, 0..3) of this thread's groups are in flight
+__device__ __forceinline__ void cp_async_wait_rt(int pending) {
+  switch (pending) {
+    case 0: cp_async_wait<0>(); break;
+    case 1: cp_async_wait<1>(); break;
+    case 2: cp_async_wait<2>(); break;
+    default: cp_async_wait<3>(); break;
+  }
+}
+
+}  // namespace greta

@@ -11,10 +11,8 @@
 //                    contents are written by the same thread that read the old
 //                    ones (greta_vllm/triton_conv.py:28-116, both kernels fused)
 //
-// Per thread: NV channels x a run of L tokens, walked in time order with the
-// last W-1 input vectors kept in registers. Loads of U consecutive tokens are
-// issued before their arithmetic so every thread keeps several 16-byte loads
-// in flight.
+// Per thread: NV channels x a run of L tokens walked in time order, with the
+// last W-1 inputs in registers; see dynconv_fwd_kernel below.
 #pragma once
 
 #include "dynconv_common.cuh"
@@ -22,7 +20,7 @@
 namespace greta {
 
 __device__ __forceinline__ bool resolve_fwd_chunk(const FwdParams& p, ChunkInfo& ci, int W) {
-  const long long cid = blockIdx.x;
+  const long long cid = blockIdx.x / p.nblk;
   const int H = W - 1;
   ci.slot = -1;
   ci.has_state = 0;
@@ -80,7 +78,7 @@ __device__ __forceinline__ bool resolve_fwd_chunk(const FwdParams& p, ChunkInfo&
     ci.hist = kHistState;
     long long slot = h.slot_raw;
     if (slot >= p.num_slots) {
-      if (p.err != nullptr && threadIdx.x == 0 && threadIdx.y == 0 && blockIdx.y == 0) atomicOr(p.err, 1);
+      if (p.err != nullptr && threadIdx.x == 0 && threadIdx.y == 0 && blockIdx.x % p.nblk == 0) atomicOr(p.err, 1);
       slot = -1;
     }
     ci.slot = slot < 0 ? -1 : slot;
@@ -133,26 +131,12 @@ __device__ __forceinline__ void load_old_state(const FwdParams& p, const ChunkIn
         sr[i].v[j] = base[(long long)(d0 + j) * p.s_d + (long long)(H - 1 - i) * p.s_h];
 }
 
-// New slot contents: tap h <- input at local position len-H+h when that is
-// inside the chunk, else the old tap len+h (zero without history).
-// Element copies only, so the state stays bit-exact
+// Write the new slot contents, given in tap order (taps[h] = tap h). The
+// values are input elements copied as they are, so the state stays bit-exact
 // (greta_vllm/triton_conv.py:102-116, greta_vllm/conv.py:61-69).
 template <typename T, int NV, int WT, int MAXH>
-__device__ __forceinline__ void store_new_state(const FwdParams& p, const ChunkInfo& ci, int d0,
-                                                int H, const Pack<T, NV> (&sr)[MAXH]) {
-  const T* xg = reinterpret_cast<const T*>(p.x);
-  Pack<T, NV> nv[MAXH];
-#pragma unroll
-  for (int h = 0; h < MAXH; ++h) {
-    zero(nv[h]);
-    if (h < H) {
-      const long long q = ci.len - H + h;
-      if (q >= 0)
-        nv[h] = ld<T, NV>(xg + (ci.x_base + q) * p.D + d0);
-      else
-        nv[h] = sel(sr, (int)(H - 1 - ci.len - h));
-    }
-  }
+__device__ __forceinline__ void store_state_taps(const FwdParams& p, const ChunkInfo& ci, int d0, int H,
+                                                 const Pack<T, NV> (&taps)[MAXH]) {
   T* base = reinterpret_cast<T*>(p.state) + ci.slot * p.s_slot;
   if constexpr (NV == kVec && WT > 1) {
     if (p.st_layout == kStDS) {
@@ -163,7 +147,7 @@ __device__ __forceinline__ void store_new_state(const FwdParams& p, const ChunkI
 #pragma unroll
         for (int j = 0; j < NV; ++j) {
           const int e = j * HH + h;
-          raw[e / NV].v[e % NV] = nv[h].v[j];
+          raw[e / NV].v[e % NV] = taps[h].v[j];
         }
 #pragma unroll
       for (int q = 0; q < HH; ++q) st<T, NV>(base + (long long)d0 * HH + q * NV, raw[q]);
@@ -174,7 +158,7 @@ __device__ __forceinline__ void store_new_state(const FwdParams& p, const ChunkI
     if (p.st_layout == kStSD) {
 #pragma unroll
       for (int h = 0; h < MAXH; ++h)
-        if (h < H) st<T, NV>(base + (long long)h * p.s_h + d0, nv[h]);
+        if (h < H) st<T, NV>(base + (long long)h * p.s_h + d0, taps[h]);
       return;
     }
   }
@@ -182,15 +166,55 @@ __device__ __forceinline__ void store_new_state(const FwdParams& p, const ChunkI
   for (int h = 0; h < MAXH; ++h)
     if (h < H)
 #pragma unroll
-      for (int j = 0; j < NV; ++j) base[(long long)(d0 + j) * p.s_d + (long long)h * p.s_h] = nv[h].v[j];
+      for (int j = 0; j < NV; ++j) base[(long long)(d0 + j) * p.s_d + (long long)h * p.s_h] = taps[h].v[j];
 }
 
+// One token's operands: the input vector, the W filter taps (reversed:
+// w[i] = tap W-1-i, the filter of the input i steps in the past) and the gate.
+template <typename T, int NV, int GV, int MAXW>
+struct TokenLoads {
+  Pack<T, NV> x, g;
+  Pack<T, GV> w[MAXW];
+};
+
+template <typename T, int NV, int GV, int MAXW>
+__device__ __forceinline__ void load_token(TokenLoads<T, NV, GV, MAXW>& o, const T* __restrict__ xg,
+                                           const T* __restrict__ wg, const T* __restrict__ gg, long long xrow,
+                                           long long orow, int D, int W, long long DC, long long f0, int d0,
+                                           bool active) {
+  zero(o.x);
+  zero(o.g);
+#pragma unroll
+  for (int i = 0; i < MAXW; ++i) zero(o.w[i]);
+  if (!active) return;
+  o.x = ld<T, NV>(xg + xrow * D + d0);
+  const T* wrow = wg + orow * W * DC + f0;
+#pragma unroll
+  for (int i = 0; i < MAXW; ++i)
+    if (i < W) o.w[i] = ld<T, GV>(wrow + (long long)(W - 1 - i) * DC);
+  if (gg != nullptr) o.g = ld<T, NV>(gg + orow * D + d0);
+}
+
+// A thread owns NV channels x a run of L consecutive tokens [rs, re) of one
+// sequence and walks it in time order: the last W-1 inputs stay in registers
+// (each x row is read once, plus a W-1 row halo per run), and the loads of
+// token t+1 are issued before the arithmetic of token t.
+//
+// Cache-slot state: per request and channel vector, ONE thread (row 0 of the
+// request's first chunk) touches the slot. It loads the old taps into its
+// history window before anything else, and writes the new taps either from
+// its final window (the whole request is in its run: decode, short chunks;
+// the window then still holds old taps for requests shorter than W-1) or
+// from the request's last W-1 inputs loaded up front (longer requests; all
+// new taps then come from the chunk). No other thread reads the slot, so no
+// barrier is needed.
+//
+// CTAs are numbered channel block fastest (blockIdx.x = chunk * nblk + block).
 template <typename T, int NV, int WT, int NORM, int GV>
 __global__ void __launch_bounds__(256) dynconv_fwd_kernel(const FwdParams p) {
   constexpr int MAXW = WT > 0 ? WT : -WT;
   constexpr int MAXH = MAXW > 1 ? MAXW - 1 : 1;
   constexpr int GC = NV / GV;
-  constexpr int U = 1;
   const int W = WT > 0 ? WT : p.W;
   const int H = W - 1;
   const int D = p.D;
@@ -200,7 +224,7 @@ __global__ void __launch_bounds__(256) dynconv_fwd_kernel(const FwdParams p) {
   ChunkInfo ci;
   if (!resolve_fwd_chunk(p, ci, W)) return;
 
-  const int d0 = (blockIdx.y * blockDim.x + threadIdx.x) * NV;
+  const int d0 = ((int)(blockIdx.x % p.nblk) * blockDim.x + threadIdx.x) * NV;
   const bool active = d0 < D;
   const int lpg = (GV == 1 && G > NV) ? G / NV : 1;
   const long long f0 = d0 / G;
@@ -213,13 +237,27 @@ __global__ void __launch_bounds__(256) dynconv_fwd_kernel(const FwdParams p) {
   T* __restrict__ yg = reinterpret_cast<T*>(p.y);
   T* __restrict__ yrg = reinterpret_cast<T*>(p.yr);
 
+  // first token's operands: independent of the state, issued first
+  TokenLoads<T, NV, GV, MAXW> nxt;
+  if (rs < re) load_token(nxt, xg, wg, gg, ci.x_base + rs, ci.o_base + rs, D, W, DC, f0, d0, active);
+
+  const bool state_head = ci.hist == kHistState && ci.head && threadIdx.y == 0;
+  const bool write_back = state_head && ci.slot >= 0 && active;
+  const bool wb_window = ci.len <= re;  // the whole request is in this thread's run
+
   Pack<T, NV> hw[MAXH];  // hw[i] = input at (current position - 1 - i)
-  if (ci.hist == kHistState && ci.head && threadIdx.y == 0) {
-    Pack<T, NV> sr[MAXH];
-    load_old_state<T, NV, WT, MAXH>(p, ci, d0, active, H, sr);
-    if (ci.slot >= 0 && active) store_new_state<T, NV, WT, MAXH>(p, ci, d0, H, sr);
+  if (state_head) {
+    Pack<T, NV> tail[MAXH];
+    if (write_back && !wb_window) {
+      // the request's last W-1 inputs (len > L >= W-1, so all are chunk rows)
 #pragma unroll
-    for (int i = 0; i < MAXH; ++i) hw[i] = sr[i];
+      for (int h = 0; h < MAXH; ++h) {
+        zero(tail[h]);
+        if (h < H) tail[h] = ld<T, NV>(xg + (ci.x_base + ci.len - H + h) * D + d0);
+      }
+    }
+    load_old_state<T, NV, WT, MAXH>(p, ci, d0, active, H, hw);
+    if (write_back && !wb_window) store_state_taps<T, NV, WT, MAXH>(p, ci, d0, H, tail);
   } else {
 #pragma unroll
     for (int i = 0; i < MAXH; ++i) {
@@ -231,74 +269,56 @@ __global__ void __launch_bounds__(256) dynconv_fwd_kernel(const FwdParams p) {
     }
   }
 
-  for (long long t0 = rs; t0 < re; t0 += U) {
-    Pack<T, NV> xr[U], gr[U];
-    Pack<T, GV> wr[U][MAXW];
+  for (long long t = rs; t < re; ++t) {
+    const TokenLoads<T, NV, GV, MAXW> cur = nxt;
+    if (t + 1 < re) load_token(nxt, xg, wg, gg, ci.x_base + t + 1, ci.o_base + t + 1, D, W, DC, f0, d0, active);
+    float acc[NV];
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      zero(xr[u]);
-      zero(gr[u]);
+    for (int c = 0; c < NV; ++c) acc[c] = 0.f;
+    // taps oldest first: i = distance into the past
 #pragma unroll
-      for (int i = 0; i < MAXW; ++i) zero(wr[u][i]);
-      const long long t = t0 + u;
-      if (t < re && active) {
-        xr[u] = ld<T, NV>(xg + (ci.x_base + t) * D + d0);
-        const T* wrow = wg + (ci.o_base + t) * W * DC + f0;
+    for (int i = MAXW - 1; i >= 0; --i) {
+      if (i < W) {
+        const Pack<T, NV>& xs = (i == 0) ? cur.x : hw[i > 0 ? i - 1 : 0];
 #pragma unroll
-        for (int i = 0; i < MAXW; ++i)
-          if (i < W) wr[u][i] = ld<T, GV>(wrow + (long long)(W - 1 - i) * DC);
-        if (gg != nullptr) gr[u] = ld<T, NV>(gg + (ci.o_base + t) * D + d0);
+        for (int c = 0; c < NV; ++c) acc[c] = fmaf(to_f(xs.v[c]), to_f(cur.w[i].v[c / GC]), acc[c]);
       }
     }
+    const long long orow = (ci.o_base + t) * D + d0;
+    if (NORM != kNormNone) {
+      if (yrg != nullptr && active) {
+        Pack<T, NV> o;
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const long long t = t0 + u;
-      if (t < re) {  // uniform across the warp
-        float acc[NV];
+        for (int c = 0; c < NV; ++c) o.v[c] = from_f<T>(acc[c]);
+        st<T, NV>(yrg + orow, o);
+      }
+      apply_norm<NORM, NV, GV>(acc, G, lpg, p.eps);
+    }
+    if (gg != nullptr) {
 #pragma unroll
-        for (int c = 0; c < NV; ++c) acc[c] = 0.f;
-        // taps oldest first: i = distance into the past
-#pragma unroll
-        for (int i = MAXW - 1; i >= 0; --i) {
-          if (i < W) {
-            if (i == 0) {
-#pragma unroll
-              for (int c = 0; c < NV; ++c) acc[c] = fmaf(to_f(xr[u].v[c]), to_f(wr[u][0].v[c / GC]), acc[c]);
-            } else {
-#pragma unroll
-              for (int c = 0; c < NV; ++c)
-                acc[c] = fmaf(to_f(hw[i > 0 ? i - 1 : 0].v[c]), to_f(wr[u][i].v[c / GC]), acc[c]);
-            }
-          }
-        }
-        const long long orow = (ci.o_base + t) * D + d0;
-        if (NORM != kNormNone) {
-          if (yrg != nullptr && active) {
-            Pack<T, NV> o;
-#pragma unroll
-            for (int c = 0; c < NV; ++c) o.v[c] = from_f<T>(acc[c]);
-            st<T, NV>(yrg + orow, o);
-          }
-          apply_norm<NORM, NV, GV>(acc, G, lpg, p.eps);
-        }
-        if (gg != nullptr) {
-#pragma unroll
-          for (int c = 0; c < NV; ++c) {
-            const float gf = to_f(gr[u].v[c]);
-            acc[c] = acc[c] * (gf * sigmoidf_(gf));
-          }
-        }
-        if (active) {
-          Pack<T, NV> o;
-#pragma unroll
-          for (int c = 0; c < NV; ++c) o.v[c] = from_f<T>(acc[c]);
-          st<T, NV>(yg + orow, o);
-        }
-#pragma unroll
-        for (int i = MAXH - 1; i > 0; --i) hw[i] = hw[i - 1];
-        hw[0] = xr[u];
+      for (int c = 0; c < NV; ++c) {
+        const float gf = to_f(cur.g.v[c]);
+        acc[c] = acc[c] * (gf * sigmoidf_(gf));
       }
     }
+    if (active) {
+      Pack<T, NV> o;
+#pragma unroll
+      for (int c = 0; c < NV; ++c) o.v[c] = from_f<T>(acc[c]);
+      st<T, NV>(yg + orow, o);
+    }
+#pragma unroll
+    for (int i = MAXH - 1; i > 0; --i) hw[i] = hw[i - 1];
+    hw[0] = cur.x;
+  }
+
+  if (write_back && wb_window) {
+    // hw[i] now holds the value at position len-1-i (old taps for negative
+    // positions), so the new tap h is hw[H-1-h]
+    Pack<T, NV> taps[MAXH];
+#pragma unroll
+    for (int h = 0; h < MAXH; ++h) taps[h] = sel(hw, H - 1 - h);
+    store_state_taps<T, NV, WT, MAXH>(p, ci, d0, H, taps);
   }
 }
 

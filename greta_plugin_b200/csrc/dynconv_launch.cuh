@@ -12,23 +12,42 @@ namespace greta {
 struct LaunchShape {
   dim3 grid;
   dim3 block;
+  int nblk = 1;     // channel blocks (blockIdx.x = chunk * nblk + channel block)
+  size_t smem = 0;  // dynamic shared memory per CTA
 };
+
+// Raise a kernel's dynamic shared-memory limit when a launch needs more than
+// the default 48 KB (large W with wide CTAs, or fp32).
+template <typename K>
+cudaError_t allow_smem(K kernel, size_t smem) {
+  if (smem <= 48 * 1024) return cudaSuccess;
+  return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+}
+
+template <typename T, int NV, int WT, int NORM, int GV>
+cudaError_t fwd_one(FwdParams p, const LaunchShape& s, cudaStream_t st) {
+  auto k = dynconv_fwd_kernel<T, NV, WT, NORM, GV>;
+  cudaError_t e = allow_smem(k, s.smem);
+  if (e != cudaSuccess) return e;
+  p.nblk = s.nblk;
+  k<<<s.grid, s.block, s.smem, st>>>(p);
+  return cudaGetLastError();
+}
 
 template <typename T, int NV, int WT, int NORM>
 cudaError_t fwd_gv(const FwdParams& p, int gv, const LaunchShape& s, cudaStream_t st) {
   if constexpr (NV == kVec) {
     switch (gv) {
-      case 8: dynconv_fwd_kernel<T, NV, WT, NORM, 8><<<s.grid, s.block, 0, st>>>(p); break;
-      case 4: dynconv_fwd_kernel<T, NV, WT, NORM, 4><<<s.grid, s.block, 0, st>>>(p); break;
-      case 2: dynconv_fwd_kernel<T, NV, WT, NORM, 2><<<s.grid, s.block, 0, st>>>(p); break;
-      case 1: dynconv_fwd_kernel<T, NV, WT, NORM, 1><<<s.grid, s.block, 0, st>>>(p); break;
+      case 8: return fwd_one<T, NV, WT, NORM, 8>(p, s, st);
+      case 4: return fwd_one<T, NV, WT, NORM, 4>(p, s, st);
+      case 2: return fwd_one<T, NV, WT, NORM, 2>(p, s, st);
+      case 1: return fwd_one<T, NV, WT, NORM, 1>(p, s, st);
       default: return cudaErrorInvalidValue;
     }
   } else {
     if (gv != 1) return cudaErrorInvalidValue;
-    dynconv_fwd_kernel<T, NV, WT, NORM, 1><<<s.grid, s.block, 0, st>>>(p);
+    return fwd_one<T, NV, WT, NORM, 1>(p, s, st);
   }
-  return cudaGetLastError();
 }
 
 template <typename T, int NV, int WT>
@@ -53,21 +72,27 @@ cudaError_t launch_fwd(const FwdParams& p, int nv, int norm, int gv, const Launc
   return fwd_norm<T, 1, -kMaxWGeneric>(p, norm, gv, s, st);
 }
 
+template <typename T, int NV, int WT, int NORM, int GV>
+cudaError_t bwd_one(BwdParams p, const LaunchShape& s, cudaStream_t st) {
+  p.nblk = s.nblk;
+  dynconv_bwd_kernel<T, NV, WT, NORM, GV><<<s.grid, s.block, 0, st>>>(p);
+  return cudaGetLastError();
+}
+
 template <typename T, int NV, int WT, int NORM>
 cudaError_t bwd_gv(const BwdParams& p, int gv, const LaunchShape& s, cudaStream_t st) {
   if constexpr (NV == kVec) {
     switch (gv) {
-      case 8: dynconv_bwd_kernel<T, NV, WT, NORM, 8><<<s.grid, s.block, 0, st>>>(p); break;
-      case 4: dynconv_bwd_kernel<T, NV, WT, NORM, 4><<<s.grid, s.block, 0, st>>>(p); break;
-      case 2: dynconv_bwd_kernel<T, NV, WT, NORM, 2><<<s.grid, s.block, 0, st>>>(p); break;
-      case 1: dynconv_bwd_kernel<T, NV, WT, NORM, 1><<<s.grid, s.block, 0, st>>>(p); break;
+      case 8: return bwd_one<T, NV, WT, NORM, 8>(p, s, st);
+      case 4: return bwd_one<T, NV, WT, NORM, 4>(p, s, st);
+      case 2: return bwd_one<T, NV, WT, NORM, 2>(p, s, st);
+      case 1: return bwd_one<T, NV, WT, NORM, 1>(p, s, st);
       default: return cudaErrorInvalidValue;
     }
   } else {
     if (gv != 1) return cudaErrorInvalidValue;
-    dynconv_bwd_kernel<T, NV, WT, NORM, 1><<<s.grid, s.block, 0, st>>>(p);
+    return bwd_one<T, NV, WT, NORM, 1>(p, s, st);
   }
-  return cudaGetLastError();
 }
 
 template <typename T, int NV, int WT>

@@ -155,6 +155,24 @@ GRETA_API int greta_dynconv_packed_state(int dtype, const void* x, const void* w
                                int64_t num_reqs, int64_t T, int64_t D, int64_t W, int64_t G,
                                int norm, float eps, int32_t* error_flags, void* stream);
 
+/* Launch paths, for greta_dynconv_set_launch_shape. */
+#define GRETA_PATH_FWD 0
+#define GRETA_PATH_BWD 1
+#define GRETA_PATH_INFERENCE 2
+#define GRETA_PATH_DECODE_ROWS 3
+#define GRETA_PATH_PACKED_PREFILL 4 /* packed batches with more than 2 tokens per request */
+#define GRETA_PATH_PACKED_DECODE 5  /* packed batches with at most 2 tokens per request */
+
+/*
+ * Tuning knob (no counterpart in the reference, whose Triton kernels are
+ * autotuned): overrides the CTA shape of one launch path for the whole
+ * process. block_x = threads along channels (multiple of 32), block_y = token
+ * runs per CTA, tokens = tokens per run (raised to at least W-1), with
+ * block_x * block_y <= 256. Any argument <= 0 restores the built-in shape.
+ * Returns GRETA_ERR_INVALID_ARG for an unknown path or a bad shape.
+ */
+GRETA_API int greta_dynconv_set_launch_shape(int path, int block_x, int block_y, int tokens);
+
 /* Mirrors supports() in greta_vllm/triton_conv.py:119-121 (plus the G <= 256 limit). */
 GRETA_API int greta_dynconv_supports(int64_t group_size, int64_t channels);
 
