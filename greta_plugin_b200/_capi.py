@@ -49,10 +49,13 @@ def lib() -> ctypes.CDLL:
                                              I64, I32, F, P, P]
     L.greta_dynconv_supports.argtypes = [I64, I64]
     L.greta_dynconv_set_launch_shape.argtypes = [I32, I32, I32, I32]
+    L.greta_dynconv_set_tma.argtypes = [I32]
+    L.greta_dynconv_device_errors.argtypes = [I32]
     L.greta_dynconv_status_string.argtypes = [I32]
     L.greta_dynconv_status_string.restype = ctypes.c_char_p
     L.greta_dynconv_version.restype = I32
-    for name in ("fwd", "bwd", "inference", "decode_rows", "packed_state", "supports", "set_launch_shape"):
+    for name in ("fwd", "bwd", "inference", "decode_rows", "packed_state", "supports", "set_launch_shape", "set_tma",
+                 "device_errors"):
         getattr(L, f"greta_dynconv_{name}").restype = I32
     _lib = L
     return L
@@ -87,6 +90,16 @@ PATH_FWD, PATH_BWD, PATH_INFERENCE, PATH_DECODE_ROWS, PATH_PACKED_PREFILL, PATH_
 def set_launch_shape(path: int, block_x: int = 0, block_y: int = 0, tokens: int = 0) -> None:
     """Override (or, with zeros, restore) the CTA shape of one launch path."""
     check("greta_dynconv_set_launch_shape", lib().greta_dynconv_set_launch_shape(path, block_x, block_y, tokens))
+
+
+def set_tma(enable: bool) -> None:
+    """Use (default) or bypass the TMA-staged forward for long token streams."""
+    lib().greta_dynconv_set_tma(1 if enable else 0)
+
+
+def device_errors(clear: bool = True) -> int:
+    """Device-side error bits of earlier kernels (synchronises the device)."""
+    return int(lib().greta_dynconv_device_errors(1 if clear else 0))
 
 
 def version() -> int:

@@ -13,4 +13,11 @@ cudaError_t launch_bwd_bf16(const BwdParams& p, int nv, int norm, int gv, const 
   return launch_bwd<__nv_bfloat16>(p, nv, norm, gv, s, st);
 }
 
+cudaError_t launch_fwd_rows_bf16(const RowsParams& p, int norm, int gv, dim3 grid, dim3 block, size_t smem,
+                                cudaStream_t st) {
+  return launch_fwd_rows<__nv_bfloat16>(p, norm, gv, grid, block, smem, st);
+}
+
+int device_errors_bf16(bool clear) { return read_device_errors(clear); }
+
 }  // namespace greta

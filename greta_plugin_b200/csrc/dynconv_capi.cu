@@ -110,6 +110,89 @@ constexpr Shape kDefaultShape[kPaths] = {
 };
 Shape g_override[kPaths] = {};
 
+// ---------------------------------------------------------------------------
+// TMA forward (dynconv_fwd_tma.cuh): applicability and shared-memory plan
+// ---------------------------------------------------------------------------
+bool g_tma_enabled = true;
+
+int num_sms() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  static int cache[64] = {0};
+  if (dev >= 0 && dev < 64 && cache[dev] > 0) return cache[dev];
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+  if (dev >= 0 && dev < 64) cache[dev] = n;
+  return n;
+}
+
+size_t a128(size_t v) { return (v + 127) & ~(size_t)127; }
+
+cudaError_t run_rows(int dtype, const RowsParams& p, int norm, int gv, dim3 grid, dim3 block, size_t smem,
+                     void* stream) {
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case GRETA_DT_F32: return launch_fwd_rows_f32(p, norm, gv, grid, block, smem, st);
+    case GRETA_DT_F16: return launch_fwd_rows_f16(p, norm, gv, grid, block, smem, st);
+    default: return launch_fwd_rows_bf16(p, norm, gv, grid, block, smem, st);
+  }
+}
+
+// Launch the row-streaming TMA forward when it applies: rows of at most 4096
+// channels in whole 256-channel blocks, 16-byte aligned tensors, filter rows
+// of whole 16-byte units, DS / SD state, at most kMaxSeqsTma sequences, and
+// room for at least two token rows in flight. Returns -1 when it does not.
+int try_rows_fwd(int dtype, RowsParams p, bool gate, int norm, void* stream) {
+  if (!g_tma_enabled) return -1;
+  const int es = esize(dtype);
+  const int64_t D = p.D, W = p.W, G = p.G, DC = D / G;
+  if (D % 256 != 0 || D > kMaxRowsD || W > kMaxWGeneric) return -1;
+  if (p.mode == kModePacked && p.nseq > kMaxSeqsTma) return -1;
+  if (p.state != nullptr && p.st_layout != kStDS && p.st_layout != kStSD) return -1;
+  for (const void* q : {p.x, p.w, p.g, (const void*)p.y, (const void*)p.yr})
+    if (!aligned(q, 16)) return -1;
+  const int64_t rowx = D * es, roww = W * DC * es;
+  if (roww % 16 != 0) return -1;
+  const bool packed = p.mode == kModePacked;
+  const size_t off_stage = packed ? a128((size_t)(p.nseq + 1) * 8) : 0;
+  const size_t budget = 200 * 1024;
+  if (off_stage >= budget) return -1;
+  const int64_t per_token = rowx + roww + (gate ? rowx : 0);
+  const int64_t inflight = (int64_t)(budget - off_stage) / per_token;
+  if (inflight < 2) return -1;
+  int S, BT;
+  if (inflight >= 8) {
+    S = 4;
+    BT = (int)(inflight / 4 < 16 ? inflight / 4 : 16);
+  } else {
+    S = (int)(inflight < kMaxStages ? inflight : kMaxStages);
+    BT = 1;
+  }
+  size_t so_w, so_g, stage;
+  for (;;) {
+    so_w = a128((size_t)BT * rowx);
+    so_g = so_w + a128((size_t)BT * roww);
+    stage = so_g + (gate ? a128((size_t)BT * rowx) : 0);
+    if (off_stage + S * stage <= budget || (BT == 1 && S == 2)) break;
+    if (BT > 1) --BT; else --S;
+  }
+  if (off_stage + S * stage > budget) return -1;
+  p.BT = BT;
+  p.stages = S;
+  p.off_bnd = 0;
+  p.off_stage = (int)off_stage;
+  p.stage_bytes = (int)stage;
+  p.so_w = (int)so_w;
+  p.so_g = (int)so_g;
+  const long long work = p.U;
+  long long grid = num_sms();
+  if (work < grid) grid = work;
+  if (grid <= 0) return GRETA_OK;
+  const size_t smem = off_stage + S * stage;
+  return finish(run_rows(dtype, p, norm, group_vec(kVec, G), dim3((unsigned)grid), dim3((unsigned)(32 + D / kVec)),
+                         smem, stream));
+}
+
 // A run must cover the W-1 history positions: a request's old slot taps are
 // then only read by row 0 of its first chunk.
 Shape shape_for(int path, int H) {
@@ -133,6 +216,17 @@ int greta_dynconv_fwd(int dtype, const void* x, const void* w, const void* gate,
   if (!x || !w || !y) return GRETA_ERR_INVALID_ARG;
   const int nv = pick_nv(dtype, D, G, {x, gate, y, yr}, w);
   if (nv == 0) return GRETA_ERR_ALIGNMENT;
+  if (nv == kVec) {
+    RowsParams tp{};
+    tp.x = x; tp.w = w; tp.g = gate; tp.y = y; tp.yr = norm != GRETA_NORM_NONE ? yr : nullptr;
+    tp.starts = cu_seqlens; tp.starts_i64 = cu_seqlens_int64 ? 1 : 0;
+    tp.mode = cu_seqlens ? kModePacked : kModeSingle;
+    tp.nseq = cu_seqlens ? num_seqs : 1;
+    tp.T = T; tp.U = T; tp.D = (int)D; tp.W = (int)W; tp.G = (int)G;
+    tp.eps = eps;
+    const int r = try_rows_fwd(dtype, tp, gate != nullptr, norm, stream);
+    if (r >= 0) return r;
+  }
   const Shape sh = shape_for(GRETA_PATH_FWD, (int)W - 1);
   FwdParams p{};
   p.x = x; p.w = w; p.g = gate; p.y = y; p.yr = norm != GRETA_NORM_NONE ? yr : nullptr;
@@ -187,6 +281,16 @@ int greta_dynconv_inference(int dtype, const void* context, const void* w, const
   if (!context || !w || !y) return GRETA_ERR_INVALID_ARG;
   const int nv = pick_nv(dtype, D, G, {context, gate, y}, w);
   if (nv == 0) return GRETA_ERR_ALIGNMENT;
+  if (nv == kVec) {
+    RowsParams tp{};
+    tp.x = context; tp.w = w; tp.g = gate; tp.y = y; tp.yr = nullptr;
+    tp.mode = kModeContext;
+    tp.nseq = B;
+    tp.T = Q; tp.U = B * Q; tp.D = (int)D; tp.W = (int)W; tp.G = (int)G;
+    tp.eps = eps;
+    const int r = try_rows_fwd(dtype, tp, gate != nullptr, norm, stream);
+    if (r >= 0) return r;
+  }
   const Shape sh = shape_for(GRETA_PATH_INFERENCE, (int)W - 1);
   FwdParams p{};
   p.x = context; p.w = w; p.g = gate; p.y = y; p.yr = nullptr;
@@ -271,9 +375,33 @@ int greta_dynconv_packed_state(int dtype, const void* x, const void* w, const vo
     p.state = nullptr;
     p.num_slots = 0;
   }
+  if (!decode_like && nv == kVec) {
+    RowsParams tp{};
+    tp.x = x; tp.w = w; tp.g = gate; tp.y = y; tp.yr = nullptr;
+    tp.starts = starts; tp.starts_i64 = 0;
+    tp.mode = kModePacked;
+    tp.nseq = num_reqs;
+    tp.T = T; tp.U = T; tp.D = (int)D; tp.W = (int)W; tp.G = (int)G;
+    tp.state = p.state; tp.s_slot = p.s_slot; tp.s_d = p.s_d; tp.s_h = p.s_h; tp.num_slots = p.num_slots;
+    tp.st_layout = p.st_layout; tp.slots = slots; tp.initial = p.initial; tp.err = error_flags;
+    tp.eps = eps;
+    const int r = try_rows_fwd(dtype, tp, gate != nullptr, norm, stream);
+    if (r >= 0) return r;
+  }
   const long long chunks = cdiv(T, p.chunk) + num_reqs;
   if (chunks * (D / 8 + 1) > INT_MAX) return GRETA_ERR_INVALID_ARG;
   return finish(run_fwd(dtype, p, nv, norm, make_shape(chunks, D, nv, sh.tx, sh.ty), stream));
+}
+
+int greta_dynconv_set_tma(int enable) {
+  g_tma_enabled = enable != 0;
+  return GRETA_OK;
+}
+
+int greta_dynconv_device_errors(int clear) {
+  const int a = device_errors_f32(clear != 0), b = device_errors_f16(clear != 0), c = device_errors_bf16(clear != 0);
+  if (a < 0 || b < 0 || c < 0) return -1;
+  return a | b | c;
 }
 
 int greta_dynconv_set_launch_shape(int path, int block_x, int block_y, int tokens) {

@@ -1,0 +1,472 @@
+// Forward of the dynamic convolution over long token streams (training
+// forward, HF inference from context, vLLM chunked prefill): row streaming
+// through the Tensor Memory Accelerator.
+//
+// Each persistent CTA (one per SM) owns a contiguous range of tokens and ALL
+// D channels. Its producer warp streams the range in stages of BT whole token
+// rows -- x rows, filter rows and gate rows are contiguous in memory, so a
+// stage is a few large cp.async.bulk copies (kilobytes each), completion
+// counted on the stage's "full" mbarrier. Its D/8 consumer threads each own
+// 8 channels for the whole range: they keep the last W-1 inputs in registers
+// across stages, read the token's operands from shared memory, compute the
+// fp32 conv + group norm + gate and store y directly. Consumer warps arrive on
+// the stage's "empty" mbarrier when done; the producer refills a stage only
+// after that.
+//
+// Sequences: a range boundary that would fall inside the first W-1 tokens of
+// a request is moved to the end of them, so every token whose history
+// reaches before its request's start lies in the CTA that holds the request's
+// first token (its head CTA). With cache-slot state (vLLM prefill) only the
+// head CTA reads the old taps (plain loads at the request's first token) and
+// it alone writes the new taps: from its register window at the request's
+// last token when the request ends in its range, else right after reading the
+// old taps, from the request's last W-1 inputs (then all taps come from the
+// chunk). Empty requests are dealt round-robin to CTAs (a slot without
+// history is cleared). So no slot is read after it is written.
+//
+// Every mbarrier wait is bounded; on a timeout the kernel records
+// kErrTimeout in the device error word and returns.
+#pragma once
+
+#include "dynconv_common.cuh"
+
+namespace greta {
+
+constexpr int kMaxStages = 8;
+constexpr int kMaxSeqsTma = 2048;   // sequence offsets held in shared memory
+constexpr int kMaxRowsD = 4096;     // widest row (D / 8 consumer threads <= 512)
+constexpr int kErrTimeout = 2;      // device error bit: an mbarrier wait gave up
+
+// Device error word of this translation unit (one per element type); read
+// and cleared on the host through greta_dynconv_device_errors.
+static __device__ int g_tma_errors = 0;
+
+struct RowsParams {
+  const void* x;
+  const void* w;
+  const void* g;
+  void* y;
+  void* yr;
+  const void* starts;
+  int starts_i64;
+  int mode;        // kModeSingle, kModePacked, kModeContext
+  long long nseq;  // sequences (PACKED) or batch rows (CONTEXT)
+  long long T;     // tokens (SINGLE / PACKED) or Q (CONTEXT)
+  long long U;     // tokens of the launch (T, or nseq * Q for CONTEXT)
+  int D, W, G;
+  int BT;      // token rows per stage
+  int stages;  // ring depth (<= kMaxStages)
+  // cache-slot state (PACKED only)
+  void* state;
+  long long s_slot, s_d, s_h, num_slots;
+  int st_layout;
+  const int* slots;
+  const signed char* initial;
+  int* err;  // slot-range error bits (may be null)
+  float eps;
+  // shared-memory layout (bytes from the dynamic base)
+  int off_bnd, off_stage, stage_bytes, so_w, so_g;
+};
+
+// ---------------------------------------------------------------------------
+// mbarrier and bulk-copy primitives (PTX)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void mbar_init(unsigned bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(unsigned bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(unsigned bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(bar) : "memory");
+}
+
+// Bounded wait for the phase with the given parity; false on timeout (~1 s).
+__device__ __forceinline__ bool mbar_wait(unsigned bar, unsigned parity) {
+  for (unsigned it = 0; it < (1u << 24); ++it) {
+    unsigned done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    if (done) return true;
+    if (it > 64) __nanosleep(64);
+  }
+  return false;
+}
+
+// global -> shared bulk copy; bytes a multiple of 16, both addresses 16-byte aligned
+__device__ __forceinline__ void bulk_g2s(unsigned dst, const void* src, unsigned bytes, unsigned bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(dst),
+      "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// ranges
+// ---------------------------------------------------------------------------
+// last s in [0, n) with bnd[s] <= v (bnd non-decreasing, bnd[0] <= v)
+__device__ __forceinline__ long long seq_of(const long long* bnd, long long n, long long v) {
+  long long lo = 0, hi = n - 1;
+  while (lo < hi) {
+    const long long mid = (lo + hi + 1) >> 1;
+    if (bnd[mid] <= v)
+      lo = mid;
+    else
+      hi = mid - 1;
+  }
+  return lo;
+}
+
+// Move a range boundary out of the first W-1 tokens of a request. The
+// requests cover tokens [ulo, uhi).
+__device__ __forceinline__ long long adjust_boundary(const RowsParams& p, const long long* bnd, long long v, int H,
+                                                     long long uhi) {
+  if (v >= uhi) return uhi;
+  if (p.mode == kModeContext || H == 0) return v;
+  long long a = 0, b = uhi;
+  if (p.mode == kModePacked) {
+    // the non-empty request containing v: the last s with bnd[s] <= v among
+    // the requests [0, nseq) has bnd[s + 1] > v
+    const long long s = seq_of(bnd, p.nseq, v);
+    a = bnd[s];
+    b = bnd[s + 1];
+  }
+  const long long local = v - a;
+  if (local > 0 && local < H) v = min(a + H, b);
+  return v;
+}
+
+// Old taps of this thread's channels, history order (o[i] = input at -1-i).
+template <typename T, int NV, int WT, int MAXH>
+__device__ __forceinline__ void rows_old_taps(const RowsParams& p, long long slot, int d0, int H,
+                                              Pack<T, NV> (&o)[MAXH]) {
+  const T* base = reinterpret_cast<const T*>(p.state) + slot * p.s_slot;
+  if constexpr (WT > 1) {
+    if (p.st_layout == kStDS) {
+      constexpr int HH = WT - 1;
+      Pack<T, NV> raw[HH];
+#pragma unroll
+      for (int q = 0; q < HH; ++q) raw[q] = ld<T, NV>(base + (long long)d0 * HH + q * NV);
+#pragma unroll
+      for (int h = 0; h < HH; ++h)
+#pragma unroll
+        for (int j = 0; j < NV; ++j) {
+          const int e = j * HH + h;
+          o[HH - 1 - h].v[j] = raw[e / NV].v[e % NV];
+        }
+      return;
+    }
+  }
+  if (p.st_layout == kStSD) {
+#pragma unroll
+    for (int i = 0; i < MAXH; ++i)
+      if (i < H) o[i] = ld<T, NV>(base + (long long)(H - 1 - i) * p.s_h + d0);
+    return;
+  }
+#pragma unroll
+  for (int i = 0; i < MAXH; ++i)
+    if (i < H)
+#pragma unroll
+      for (int j = 0; j < NV; ++j) o[i].v[j] = base[(long long)(d0 + j) * p.s_d + (long long)(H - 1 - i) * p.s_h];
+}
+
+// Write new taps (tap order: taps[h] = tap h) of this thread's channels.
+template <typename T, int NV, int WT, int MAXH>
+__device__ __forceinline__ void rows_store_taps(const RowsParams& p, long long slot, int d0, int H,
+                                                const Pack<T, NV> (&taps)[MAXH]) {
+  T* base = reinterpret_cast<T*>(p.state) + slot * p.s_slot;
+  if constexpr (WT > 1) {
+    if (p.st_layout == kStDS) {
+      constexpr int HH = WT - 1;
+      Pack<T, NV> raw[HH];
+#pragma unroll
+      for (int h = 0; h < HH; ++h)
+#pragma unroll
+        for (int j = 0; j < NV; ++j) {
+          const int e = j * HH + h;
+          raw[e / NV].v[e % NV] = taps[h].v[j];
+        }
+#pragma unroll
+      for (int q = 0; q < HH; ++q) st<T, NV>(base + (long long)d0 * HH + q * NV, raw[q]);
+      return;
+    }
+  }
+  if (p.st_layout == kStSD) {
+#pragma unroll
+    for (int h = 0; h < MAXH; ++h)
+      if (h < H) st<T, NV>(base + (long long)h * p.s_h + d0, taps[h]);
+    return;
+  }
+#pragma unroll
+  for (int h = 0; h < MAXH; ++h)
+    if (h < H)
+#pragma unroll
+      for (int j = 0; j < NV; ++j) base[(long long)(d0 + j) * p.s_d + (long long)h * p.s_h] = taps[h].v[j];
+}
+
+// ---------------------------------------------------------------------------
+// the kernel
+// ---------------------------------------------------------------------------
+template <typename T, int WT, int NORM, int GV>
+__global__ void __launch_bounds__(32 + kMaxRowsD / kVec, 1) dynconv_fwd_rows_kernel(const RowsParams p) {
+  constexpr int NV = kVec;
+  constexpr int MAXW = WT > 0 ? WT : -WT;
+  constexpr int MAXH = MAXW > 1 ? MAXW - 1 : 1;
+  constexpr int GC = NV / GV;
+  constexpr int ES = (int)sizeof(T);
+  using PX = Pack<T, NV>;
+  using PW = Pack<T, GV>;
+  const int W = WT > 0 ? WT : p.W;
+  const int H = W - 1;
+  const int D = p.D;
+  const int G = p.G;
+  const long long DC = D / G;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nconsw = (int)(blockDim.x >> 5) - 1;  // consumer warps
+  const int S = p.stages;
+
+  extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ __align__(8) unsigned long long bars[2 * kMaxStages];
+  const unsigned full0 = smem_addr(&bars[0]), empty0 = smem_addr(&bars[kMaxStages]);
+  long long* bnd = reinterpret_cast<long long*>(smem + p.off_bnd);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, nconsw);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
+  if (p.mode == kModePacked)
+    for (long long i = threadIdx.x; i <= p.nseq; i += blockDim.x)
+      bnd[i] = clampll(load_idx(p.starts, i, p.starts_i64), 0, p.T);
+  __syncthreads();
+  if (p.mode == kModePacked && threadIdx.x == 0) {
+    // make the offsets non-decreasing (a decreasing offset = an empty request)
+    for (long long i = 1; i <= p.nseq; ++i)
+      if (bnd[i] < bnd[i - 1]) bnd[i] = bnd[i - 1];
+  }
+  __syncthreads();
+
+  // this CTA's token range inside the covered tokens [ulo, uhi)
+  const long long ulo = p.mode == kModePacked ? bnd[0] : 0;
+  const long long uhi = p.mode == kModePacked ? bnd[p.nseq] : p.U;
+  const long long nominal = (uhi - ulo + gridDim.x - 1) / gridDim.x;
+  const long long u0 = adjust_boundary(p, bnd, ulo + (long long)blockIdx.x * nominal, H, uhi);
+  const long long u1 = adjust_boundary(p, bnd, ulo + (long long)(blockIdx.x + 1) * nominal, H, uhi);
+  const long long ntiles = u1 > u0 ? (u1 - u0 + p.BT - 1) / p.BT : 0;
+
+  const T* __restrict__ xg = reinterpret_cast<const T*>(p.x);
+  const T* __restrict__ wg = reinterpret_cast<const T*>(p.w);
+  const T* __restrict__ gg = reinterpret_cast<const T*>(p.g);
+  const long long xrow_b = p.mode == kModeContext ? p.T + H : 0;  // context rows per batch row
+
+  if (warp == 0) {
+    // =========================== producer ===========================
+    if (lane != 0) return;
+    const unsigned rowx = (unsigned)(D * ES), roww = (unsigned)(W * DC * ES);
+    for (long long i = 0; i < ntiles; ++i) {
+      const int s = (int)(i % S);
+      const unsigned par = (unsigned)((i / S) & 1);
+      if (i >= S && !mbar_wait(empty0 + 8 * s, par ^ 1u)) {
+        atomicOr(&g_tma_errors, kErrTimeout);
+        return;
+      }
+      const long long t0 = u0 + i * p.BT;
+      const int n = (int)min((long long)p.BT, u1 - t0);
+      const unsigned bar = full0 + 8 * s;
+      const unsigned sb = smem_addr(smem + p.off_stage + (size_t)s * p.stage_bytes);
+      mbar_arrive_expect_tx(bar, (unsigned)n * (rowx + roww + (gg != nullptr ? rowx : 0u)));
+      if (p.mode == kModeContext) {
+        for (int j = 0; j < n; ++j) {
+          const long long u = t0 + j, b = u / p.T, q = u % p.T;
+          bulk_g2s(sb + j * rowx, xg + (b * xrow_b + H + q) * D, rowx, bar);
+        }
+      } else {
+        bulk_g2s(sb, xg + t0 * D, (unsigned)n * rowx, bar);
+      }
+      bulk_g2s(sb + p.so_w, wg + t0 * W * DC, (unsigned)n * roww, bar);
+      if (gg != nullptr) bulk_g2s(sb + p.so_g, gg + t0 * D, (unsigned)n * rowx, bar);
+    }
+    return;
+  }
+
+  // =========================== consumers ===========================
+  const int d0 = ((int)threadIdx.x - 32) * NV;
+  const long long f0 = d0 / G;
+  const int lpg = (GV == 1 && G > NV) ? G / NV : 1;
+  T* __restrict__ yg = reinterpret_cast<T*>(p.y);
+  T* __restrict__ yrg = reinterpret_cast<T*>(p.yr);
+  const bool has_state = p.state != nullptr;
+
+  // empty requests, dealt round-robin: a slot without history is cleared
+  if (has_state)
+    for (long long s = blockIdx.x; s < p.nseq; s += gridDim.x)
+      if (bnd[s + 1] == bnd[s]) {
+        long long sl = p.slots[s];
+        if (sl >= p.num_slots) {
+          if (p.err != nullptr && d0 == 0) atomicOr(p.err, 1);
+          sl = -1;
+        }
+        if (sl >= 0 && p.initial[s] == 0) {
+          PX z[MAXH];
+#pragma unroll
+          for (int h = 0; h < MAXH; ++h) zero(z[h]);
+          rows_store_taps<T, NV, WT, MAXH>(p, sl, d0, H, z);
+        }
+      }
+
+  // request bookkeeping (PACKED / SINGLE): current request [ra, rb)
+  long long sq = 0, ra = 0, rb = uhi;
+  long long slot = -1;
+  bool head_here = false;  // the current request's first token is in this CTA
+  PX hw[MAXH];             // hw[i] = input at (current token - 1 - i)
+#pragma unroll
+  for (int i = 0; i < MAXH; ++i) zero(hw[i]);
+
+  auto find_request = [&](long long u) {
+    if (p.mode == kModePacked) {
+      sq = seq_of(bnd, p.nseq, u);
+      ra = bnd[sq];
+      rb = bnd[sq + 1];
+    }
+  };
+
+  // First token of a request: history = old taps (or zeros).
+  auto begin_request = [&]() {
+    head_here = true;
+    slot = -1;
+#pragma unroll
+    for (int i = 0; i < MAXH; ++i) zero(hw[i]);
+    if (!has_state) return;
+    long long sl = p.slots[sq];
+    if (sl >= p.num_slots) {
+      if (p.err != nullptr && d0 == 0) atomicOr(p.err, 1);
+      sl = -1;
+    }
+    slot = sl < 0 ? -1 : sl;
+    if (slot >= 0 && p.initial[sq] != 0) rows_old_taps<T, NV, WT, MAXH>(p, slot, d0, H, hw);
+    if (slot >= 0 && rb > u1) {
+      // the request continues past this CTA: its new taps are its last W-1
+      // inputs (it has more than W-1 tokens), written now, after the old
+      // taps were read
+      PX taps[MAXH];
+#pragma unroll
+      for (int h = 0; h < MAXH; ++h) {
+        zero(taps[h]);
+        if (h < H) taps[h] = ld<T, NV>(xg + (rb - H + h) * D + d0);
+      }
+      rows_store_taps<T, NV, WT, MAXH>(p, slot, d0, H, taps);
+      slot = -1;  // written
+    }
+  };
+
+  if (u0 < u1) {
+    if (p.mode == kModeContext) {
+      const long long b = u0 / p.T, q = u0 % p.T;
+#pragma unroll
+      for (int i = 0; i < MAXH; ++i)
+        if (i < H) hw[i] = ld<T, NV>(xg + (b * xrow_b + H + q - 1 - i) * D + d0);
+    } else {
+      find_request(u0);
+      if (u0 == ra) {
+        begin_request();
+      } else {
+        // mid-request start: the boundary rule guarantees u0 - ra >= W-1
+#pragma unroll
+        for (int i = 0; i < MAXH; ++i)
+          if (i < H) hw[i] = ld<T, NV>(xg + (u0 - 1 - i) * D + d0);
+      }
+    }
+  }
+
+  for (long long i = 0; i < ntiles; ++i) {
+    const int s = (int)(i % S);
+    const unsigned par = (unsigned)((i / S) & 1);
+    if (!mbar_wait(full0 + 8 * s, par)) {
+      if (lane == 0) atomicOr(&g_tma_errors, kErrTimeout);
+      return;
+    }
+    const unsigned char* stg = smem + p.off_stage + (size_t)s * p.stage_bytes;
+    const long long t0 = u0 + i * p.BT;
+    const int n = (int)min((long long)p.BT, u1 - t0);
+    for (int j = 0; j < n; ++j) {
+      const long long u = t0 + j;
+      if (p.mode == kModeContext) {
+        if (u % p.T == 0 && u != u0) {  // a new batch row: its history is its context
+          const long long b = u / p.T;
+#pragma unroll
+          for (int k = 0; k < MAXH; ++k)
+            if (k < H) hw[k] = ld<T, NV>(xg + (b * xrow_b + H - 1 - k) * D + d0);
+        }
+      } else if (u >= rb) {
+        find_request(u);  // skips empty requests
+        begin_request();
+      }
+      const PX xc = *reinterpret_cast<const PX*>(stg + (size_t)j * D * ES + (size_t)d0 * ES);
+      const unsigned char* wrow = stg + p.so_w + (size_t)j * W * DC * ES;
+      PW wc[MAXW];
+#pragma unroll
+      for (int k = 0; k < MAXW; ++k) {
+        zero(wc[k]);
+        if (k < W) wc[k] = *reinterpret_cast<const PW*>(wrow + ((W - 1 - k) * DC + f0) * ES);
+      }
+      float acc[NV];
+#pragma unroll
+      for (int c = 0; c < NV; ++c) acc[c] = 0.f;
+#pragma unroll
+      for (int k = MAXW - 1; k >= 0; --k) {
+        if (k < W) {
+          const PX& xv = (k == 0) ? xc : hw[k > 0 ? k - 1 : 0];
+#pragma unroll
+          for (int c = 0; c < NV; ++c) acc[c] = fmaf(to_f(xv.v[c]), to_f(wc[k].v[c / GC]), acc[c]);
+        }
+      }
+      const long long orow = u * D + d0;
+      if (NORM != kNormNone) {
+        if (yrg != nullptr) {
+          PX o;
+#pragma unroll
+          for (int c = 0; c < NV; ++c) o.v[c] = from_f<T>(acc[c]);
+          st<T, NV>(yrg + orow, o);
+        }
+        apply_norm<NORM, NV, GV>(acc, G, lpg, p.eps);
+      }
+      if (gg != nullptr) {
+        const PX gv = *reinterpret_cast<const PX*>(stg + p.so_g + (size_t)j * D * ES + (size_t)d0 * ES);
+#pragma unroll
+        for (int c = 0; c < NV; ++c) {
+          const float gf = to_f(gv.v[c]);
+          acc[c] = acc[c] * (gf * sigmoidf_(gf));
+        }
+      }
+      {
+        PX o;
+#pragma unroll
+        for (int c = 0; c < NV; ++c) o.v[c] = from_f<T>(acc[c]);
+        st<T, NV>(yg + orow, o);
+      }
+#pragma unroll
+      for (int k = MAXH - 1; k > 0; --k) hw[k] = hw[k - 1];
+      hw[0] = xc;
+      if (has_state && head_here && slot >= 0 && u == rb - 1) {
+        // the request ends here: hw[k] holds the input at rb-1-k (old taps for
+        // positions before ra), so the new tap h is hw[H-1-h]
+        PX taps[MAXH];
+#pragma unroll
+        for (int h = 0; h < MAXH; ++h) taps[h] = sel(hw, H - 1 - h);
+        rows_store_taps<T, NV, WT, MAXH>(p, slot, d0, H, taps);
+        slot = -1;
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(empty0 + 8 * s);
+  }
+}
+
+}  // namespace greta

@@ -6,6 +6,7 @@
 
 #include "dynconv_bwd.cuh"
 #include "dynconv_fwd.cuh"
+#include "dynconv_fwd_tma.cuh"
 
 namespace greta {
 
@@ -116,6 +117,56 @@ cudaError_t launch_bwd(const BwdParams& p, int nv, int norm, int gv, const Launc
   return bwd_norm<T, 1, -kMaxWGeneric>(p, norm, gv, s, st);
 }
 
+template <typename T, int WT, int NORM, int GV>
+cudaError_t rows_one(const RowsParams& p, dim3 grid, dim3 block, size_t smem, cudaStream_t st) {
+  auto k = dynconv_fwd_rows_kernel<T, WT, NORM, GV>;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  k<<<grid, block, smem, st>>>(p);
+  return cudaGetLastError();
+}
+
+template <typename T, int WT, int NORM>
+cudaError_t rows_gv(const RowsParams& p, int gv, dim3 grid, dim3 block, size_t smem, cudaStream_t st) {
+  switch (gv) {
+    case 8: return rows_one<T, WT, NORM, 8>(p, grid, block, smem, st);
+    case 4: return rows_one<T, WT, NORM, 4>(p, grid, block, smem, st);
+    case 2: return rows_one<T, WT, NORM, 2>(p, grid, block, smem, st);
+    case 1: return rows_one<T, WT, NORM, 1>(p, grid, block, smem, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+template <typename T, int WT>
+cudaError_t rows_norm(const RowsParams& p, int norm, int gv, dim3 grid, dim3 block, size_t smem, cudaStream_t st) {
+  switch (norm) {
+    case kNormNone: return rows_gv<T, WT, kNormNone>(p, gv, grid, block, smem, st);
+    case kNormPlain: return rows_gv<T, WT, kNormPlain>(p, gv, grid, block, smem, st);
+    case kNormStable: return rows_gv<T, WT, kNormStable>(p, gv, grid, block, smem, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+template <typename T>
+cudaError_t launch_fwd_rows(const RowsParams& p, int norm, int gv, dim3 grid, dim3 block, size_t smem,
+                            cudaStream_t st) {
+  if (p.W == 4) return rows_norm<T, 4>(p, norm, gv, grid, block, smem, st);
+  if (p.W == 7) return rows_norm<T, 7>(p, norm, gv, grid, block, smem, st);
+  if (p.W <= 8) return rows_norm<T, -8>(p, norm, gv, grid, block, smem, st);
+  return rows_norm<T, -kMaxWGeneric>(p, norm, gv, grid, block, smem, st);
+}
+
+// Read (and clear) this translation unit's device error word.
+inline int read_device_errors(bool clear) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_tma_errors, sizeof(int)) != cudaSuccess) return -1;
+  if (clear && v != 0) {
+    const int z = 0;
+    cudaMemcpyToSymbol(g_tma_errors, &z, sizeof(int));
+  }
+  return v;
+}
+
 // Entry points defined by the per-dtype translation units.
 cudaError_t launch_fwd_f32(const FwdParams&, int, int, int, const LaunchShape&, cudaStream_t);
 cudaError_t launch_fwd_f16(const FwdParams&, int, int, int, const LaunchShape&, cudaStream_t);
@@ -123,5 +174,11 @@ cudaError_t launch_fwd_bf16(const FwdParams&, int, int, int, const LaunchShape&,
 cudaError_t launch_bwd_f32(const BwdParams&, int, int, int, const LaunchShape&, cudaStream_t);
 cudaError_t launch_bwd_f16(const BwdParams&, int, int, int, const LaunchShape&, cudaStream_t);
 cudaError_t launch_bwd_bf16(const BwdParams&, int, int, int, const LaunchShape&, cudaStream_t);
+cudaError_t launch_fwd_rows_f32(const RowsParams&, int, int, dim3, dim3, size_t, cudaStream_t);
+cudaError_t launch_fwd_rows_f16(const RowsParams&, int, int, dim3, dim3, size_t, cudaStream_t);
+cudaError_t launch_fwd_rows_bf16(const RowsParams&, int, int, dim3, dim3, size_t, cudaStream_t);
+int device_errors_f32(bool clear);
+int device_errors_f16(bool clear);
+int device_errors_bf16(bool clear);
 
 }  // namespace greta

@@ -173,6 +173,24 @@ GRETA_API int greta_dynconv_packed_state(int dtype, const void* x, const void* w
  */
 GRETA_API int greta_dynconv_set_launch_shape(int path, int block_x, int block_y, int tokens);
 
+/*
+ * Selects the forward implementation for long token streams (no counterpart
+ * in the reference): enable != 0 (the default) stages operands through the
+ * Tensor Memory Accelerator where the shapes allow it (D a multiple of 256,
+ * 16-byte aligned rows, DS/SD state layouts, at most 2048 sequences,
+ * prefill-like batches); 0 always uses the register-staged kernels. Both give
+ * the same results. Process-wide; returns GRETA_OK.
+ */
+GRETA_API int greta_dynconv_set_tma(int enable);
+
+/*
+ * Device-side error bits recorded by earlier kernels of this library on the
+ * current device (bit 1: a pipeline wait timed out and the kernel returned
+ * early). Synchronises the device; clear != 0 resets the bits. Returns the
+ * bits, or -1 when they cannot be read. For debugging and tests.
+ */
+GRETA_API int greta_dynconv_device_errors(int clear);
+
 /* Mirrors supports() in greta_vllm/triton_conv.py:119-121 (plus the G <= 256 limit). */
 GRETA_API int greta_dynconv_supports(int64_t group_size, int64_t channels);
 

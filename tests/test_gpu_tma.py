@@ -1,0 +1,131 @@
+"""The TMA-staged forward (long token streams) against the register-staged
+forward and the oracle: both implementations run the same arithmetic, so
+their outputs must be bit-identical; the kernels must record no device error
+(a pipeline wait that timed out)."""
+import numpy as np
+import pytest
+import torch
+
+from gpu_helpers import DEV, assert_close, rand, ragged_cu, to_np
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture
+def capi():
+    from greta_plugin_b200 import _capi
+
+    _capi.device_errors(clear=True)
+    yield _capi
+    _capi.set_tma(True)
+    assert _capi.device_errors(clear=True) == 0
+
+
+def both(capi, fn):
+    capi.set_tma(True)
+    a = fn()
+    torch.cuda.synchronize()
+    capi.set_tma(False)
+    b = fn()
+    torch.cuda.synchronize()
+    capi.set_tma(True)
+    return a, b
+
+
+def _same(a, b):
+    if isinstance(a, (tuple, list)):
+        for u, v in zip(a, b):
+            _same(u, v)
+    elif a is not None:
+        assert torch.equal(a, b), "TMA and register paths differ"
+
+
+@pytest.mark.parametrize("W,G,norm,gate_on,dtype", [
+    (4, 1, False, False, torch.bfloat16), (4, 1, True, True, torch.bfloat16), (7, 128, True, True, torch.bfloat16),
+    (3, 4, False, True, torch.float16), (7, 16, True, False, torch.float32), (5, 2, True, True, torch.bfloat16),
+    (12, 8, False, True, torch.bfloat16), (4, 64, True, True, torch.bfloat16),
+])
+def test_training_forward(capi, W, G, norm, gate_on, dtype):
+    from greta_plugin_b200.dynamic_conv import dynconv_fwd
+
+    g = torch.Generator().manual_seed(W * 100 + G)
+    lens = [1, 2, 70, 5, 300, 0, 64]
+    T, D = sum(lens), 512
+    x = rand(g, 1, T, D, dtype=dtype)
+    w = rand(g, T, W, D // G, scale=0.5, dtype=dtype)
+    gate = rand(g, 1, T, D, dtype=dtype) if gate_on else None
+    cu = ragged_cu(lens)
+    xd, wd, gd, cud = x.to(DEV), w.to(DEV), None if gate is None else gate.to(DEV), cu.to(DEV)
+    (y1, yr1, _, _), (y2, yr2, _, _) = both(
+        capi, lambda: dynconv_fwd(xd, wd, gd, cud, G, norm=norm, save_pre=True))
+    _same((y1, yr1), (y2, yr2))
+    yo, _ = oracle.fwd(to_np(x[0]), to_np(w), to_np(gate[0]) if gate_on else None, cu.numpy(), G, int(norm))
+    assert_close(y1[0], yo, dtype)
+
+
+def test_training_forward_single_sequence(capi):
+    from greta_plugin_b200.dynamic_conv import dynconv_fwd
+
+    g = torch.Generator().manual_seed(1)
+    T, D, W = 777, 1024, 4
+    x, w = rand(g, 1, T, D).to(DEV), rand(g, T, W, D, scale=0.5).to(DEV)
+    a, b = both(capi, lambda: dynconv_fwd(x, w, None, None, 1)[0])
+    _same(a, b)
+    yo, _ = oracle.fwd(to_np(x[0]), to_np(w), None, None, 1, 0)
+    assert_close(a[0], yo, torch.bfloat16)
+
+
+@pytest.mark.parametrize("W,G,norm,gate_on", [(4, 1, False, False), (7, 128, True, True), (3, 8, True, False)])
+def test_inference_from_context(capi, W, G, norm, gate_on):
+    from greta_plugin_b200 import dynamic_causal_conv1d_inference
+
+    g = torch.Generator().manual_seed(W + G)
+    B, Q, D = 3, 129, 512
+    ctx = rand(g, B, Q + W - 1, D).to(DEV)
+    w = rand(g, B, Q, W, D // G, scale=0.5).to(DEV)
+    gate = rand(g, B, Q, D).to(DEV) if gate_on else None
+    a, b = both(capi, lambda: dynamic_causal_conv1d_inference(ctx, w, gate, G, norm))
+    _same(a, b)
+    yo = oracle.inference(to_np(ctx), to_np(w), to_np(gate), G, int(norm))
+    assert_close(a, yo, torch.bfloat16)
+
+
+@pytest.mark.parametrize("layout", ["DS", "SD"])
+@pytest.mark.parametrize("W,G", [(4, 1), (7, 128), (4, 8), (2, 256)])
+def test_packed_prefill_with_state(capi, layout, W, G):
+    """Prefill-like packed batch (T > 2N) with slot history: the TMA path
+    must match the register path bit for bit, including the new slot state."""
+    from greta_plugin_b200 import packed_dynamic_conv_triton
+
+    g = torch.Generator().manual_seed(W * 7 + G)
+    lens = [1, 1, 2, W - 1, 90, 33, 200, 0, 5]
+    slots = [3, -1, 7, 0, 11, 5, 2, 9, 4]
+    init = [1, 1, 0, 1, 1, 0, 1, 0, 1]
+    T, D, n_slots = sum(lens), 512, 12
+    x = rand(g, T, D).to(DEV)
+    w = rand(g, T, W, D // G, scale=0.5).to(DEV)
+    gate = rand(g, T, D).to(DEV)
+    logical = rand(g, n_slots, D, W - 1)
+    starts = torch.tensor([0] + list(np.cumsum(lens)), dtype=torch.int32, device=DEV)
+    sl = torch.tensor(slots, dtype=torch.int32, device=DEV)
+    ini = torch.tensor(init, dtype=torch.int8, device=DEV)
+
+    def make_state():
+        if layout == "DS":
+            return logical.to(DEV).contiguous()
+        return logical.transpose(1, 2).contiguous().to(DEV).transpose(1, 2)
+
+    sa, sb = make_state(), make_state()
+    capi.set_tma(True)
+    ya = packed_dynamic_conv_triton(x, w, gate, sa, starts, sl, ini, G)
+    capi.set_tma(False)
+    yb = packed_dynamic_conv_triton(x, w, gate, sb, starts, sl, ini, G)
+    capi.set_tma(True)
+    torch.cuda.synchronize()
+    assert torch.equal(ya, yb)
+    assert torch.equal(sa, sb)
+    yo, so = oracle.packed(to_np(x), to_np(w), to_np(gate), to_np(logical), starts.cpu().numpy(), np.array(slots),
+                           np.array(init), G, 2)
+    assert_close(ya, yo, torch.bfloat16)
+    assert np.array_equal(sa.float().cpu().numpy(), so)
