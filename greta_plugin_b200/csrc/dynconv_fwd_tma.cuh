@@ -270,17 +270,22 @@ __global__ void __launch_bounds__(32 + kMaxRowsD / kVec, 1) dynconv_fwd_rows_ker
     // =========================== producer ===========================
     if (lane != 0) return;
     const unsigned rowx = (unsigned)(D * ES), roww = (unsigned)(W * DC * ES);
-    for (long long i = 0; i < ntiles; ++i) {
-      const int s = (int)(i % S);
-      const unsigned par = (unsigned)((i / S) & 1);
+    const unsigned sb0 = smem_addr(smem + p.off_stage);
+    int s = 0;
+    unsigned par = 0;  // parity of the stage's current use
+    long long t0 = u0;
+    for (long long i = 0; i < ntiles; ++i, t0 += p.BT) {
       if (i >= S && !mbar_wait(empty0 + 8 * s, par ^ 1u)) {
         atomicOr(&g_tma_errors, kErrTimeout);
         return;
       }
-      const long long t0 = u0 + i * p.BT;
       const int n = (int)min((long long)p.BT, u1 - t0);
       const unsigned bar = full0 + 8 * s;
-      const unsigned sb = smem_addr(smem + p.off_stage + (size_t)s * p.stage_bytes);
+      const unsigned sb = sb0 + (unsigned)(s * p.stage_bytes);
+      if (++s == S) {
+        s = 0;
+        par ^= 1u;
+      }
       mbar_arrive_expect_tx(bar, (unsigned)n * (rowx + roww + (gg != nullptr ? rowx : 0u)));
       if (p.mode == kModeContext) {
         for (int j = 0; j < n; ++j) {
@@ -385,60 +390,102 @@ __global__ void __launch_bounds__(32 + kMaxRowsD / kVec, 1) dynconv_fwd_rows_ker
     }
   }
 
-  for (long long i = 0; i < ntiles; ++i) {
-    const int s = (int)(i % S);
-    const unsigned par = (unsigned)((i / S) & 1);
+  // History window in registers. For W <= 4 it is kept as fp32 (each input is
+  // converted once); wider windows stay in the I/O type. The fp32 copy of a
+  // bf16 / fp16 / fp32 input converts back exactly, so the slot write-back
+  // remains a bit copy.
+  constexpr bool kFloatWin = MAXH <= 3;
+  float hf[kFloatWin ? MAXH : 1][NV];
+  auto sync_window = [&]() {
+    if constexpr (kFloatWin) {
+#pragma unroll
+      for (int k = 0; k < MAXH; ++k)
+#pragma unroll
+        for (int c = 0; c < NV; ++c) hf[k][c] = to_f(hw[k].v[c]);
+    }
+  };
+  sync_window();
+
+  const int rowx = D * ES, roww = W * DC * ES;
+  int koff[MAXW];  // byte offset of the filter of the input k steps back
+#pragma unroll
+  for (int k = 0; k < MAXW; ++k) koff[k] = (k < W ? (W - 1 - k) : 0) * (int)DC * ES;
+  T* yp = yg + u0 * D + d0;
+  T* yrp = yrg != nullptr ? yrg + u0 * D + d0 : nullptr;
+  int s = 0;
+  unsigned par = 0;
+  long long t0 = u0;
+  for (long long i = 0; i < ntiles; ++i, t0 += p.BT) {
     if (!mbar_wait(full0 + 8 * s, par)) {
       if (lane == 0) atomicOr(&g_tma_errors, kErrTimeout);
       return;
     }
-    const unsigned char* stg = smem + p.off_stage + (size_t)s * p.stage_bytes;
-    const long long t0 = u0 + i * p.BT;
+    const unsigned char* stg = smem + p.off_stage + s * p.stage_bytes;
+    const int cur_s = s;
+    if (++s == S) {
+      s = 0;
+      par ^= 1u;
+    }
     const int n = (int)min((long long)p.BT, u1 - t0);
-    for (int j = 0; j < n; ++j) {
+    const unsigned char* xsp = stg + d0 * ES;
+    const unsigned char* wsp = stg + p.so_w + f0 * ES;
+    const unsigned char* gsp = stg + p.so_g + d0 * ES;
+    for (int j = 0; j < n; ++j, xsp += rowx, wsp += roww, gsp += rowx, yp += D) {
       const long long u = t0 + j;
       if (p.mode == kModeContext) {
-        if (u % p.T == 0 && u != u0) {  // a new batch row: its history is its context
+        if (u != u0 && u % p.T == 0) {  // a new batch row: its history is its context
           const long long b = u / p.T;
 #pragma unroll
           for (int k = 0; k < MAXH; ++k)
             if (k < H) hw[k] = ld<T, NV>(xg + (b * xrow_b + H - 1 - k) * D + d0);
+          sync_window();
         }
       } else if (u >= rb) {
         find_request(u);  // skips empty requests
         begin_request();
+        sync_window();
       }
-      const PX xc = *reinterpret_cast<const PX*>(stg + (size_t)j * D * ES + (size_t)d0 * ES);
-      const unsigned char* wrow = stg + p.so_w + (size_t)j * W * DC * ES;
+      const PX xc = *reinterpret_cast<const PX*>(xsp);
       PW wc[MAXW];
 #pragma unroll
       for (int k = 0; k < MAXW; ++k) {
         zero(wc[k]);
-        if (k < W) wc[k] = *reinterpret_cast<const PW*>(wrow + ((W - 1 - k) * DC + f0) * ES);
+        if (k < W) wc[k] = *reinterpret_cast<const PW*>(wsp + koff[k]);
       }
+      float xf[NV];
+#pragma unroll
+      for (int c = 0; c < NV; ++c) xf[c] = to_f(xc.v[c]);
       float acc[NV];
 #pragma unroll
       for (int c = 0; c < NV; ++c) acc[c] = 0.f;
 #pragma unroll
       for (int k = MAXW - 1; k >= 0; --k) {
         if (k < W) {
-          const PX& xv = (k == 0) ? xc : hw[k > 0 ? k - 1 : 0];
 #pragma unroll
-          for (int c = 0; c < NV; ++c) acc[c] = fmaf(to_f(xv.v[c]), to_f(wc[k].v[c / GC]), acc[c]);
+          for (int c = 0; c < NV; ++c) {
+            float xv;
+            if (k == 0)
+              xv = xf[c];
+            else if constexpr (kFloatWin)
+              xv = hf[k > 0 ? k - 1 : 0][c];
+            else
+              xv = to_f(hw[k > 0 ? k - 1 : 0].v[c]);
+            acc[c] = fmaf(xv, to_f(wc[k].v[c / GC]), acc[c]);
+          }
         }
       }
-      const long long orow = u * D + d0;
       if (NORM != kNormNone) {
-        if (yrg != nullptr) {
+        if (yrp != nullptr) {
           PX o;
 #pragma unroll
           for (int c = 0; c < NV; ++c) o.v[c] = from_f<T>(acc[c]);
-          st<T, NV>(yrg + orow, o);
+          st<T, NV>(yrp, o);
+          yrp += D;
         }
         apply_norm<NORM, NV, GV>(acc, G, lpg, p.eps);
       }
       if (gg != nullptr) {
-        const PX gv = *reinterpret_cast<const PX*>(stg + p.so_g + (size_t)j * D * ES + (size_t)d0 * ES);
+        const PX gv = *reinterpret_cast<const PX*>(gsp);
 #pragma unroll
         for (int c = 0; c < NV; ++c) {
           const float gf = to_f(gv.v[c]);
@@ -449,15 +496,30 @@ __global__ void __launch_bounds__(32 + kMaxRowsD / kVec, 1) dynconv_fwd_rows_ker
         PX o;
 #pragma unroll
         for (int c = 0; c < NV; ++c) o.v[c] = from_f<T>(acc[c]);
-        st<T, NV>(yg + orow, o);
+        st<T, NV>(yp, o);
       }
+      if constexpr (kFloatWin) {
 #pragma unroll
-      for (int k = MAXH - 1; k > 0; --k) hw[k] = hw[k - 1];
-      hw[0] = xc;
+        for (int k = MAXH - 1; k > 0; --k)
+#pragma unroll
+          for (int c = 0; c < NV; ++c) hf[k][c] = hf[k - 1][c];
+#pragma unroll
+        for (int c = 0; c < NV; ++c) hf[0][c] = xf[c];
+      } else {
+#pragma unroll
+        for (int k = MAXH - 1; k > 0; --k) hw[k] = hw[k - 1];
+        hw[0] = xc;
+      }
       if (has_state && head_here && slot >= 0 && u == rb - 1) {
-        // the request ends here: hw[k] holds the input at rb-1-k (old taps for
-        // positions before ra), so the new tap h is hw[H-1-h]
+        // the request ends here: the window holds the input at rb-1-k (old
+        // taps for positions before ra), so the new tap h is window[H-1-h]
         PX taps[MAXH];
+        if constexpr (kFloatWin) {
+#pragma unroll
+          for (int k = 0; k < MAXH; ++k)
+#pragma unroll
+            for (int c = 0; c < NV; ++c) hw[k].v[c] = from_f<T>(hf[k][c]);
+        }
 #pragma unroll
         for (int h = 0; h < MAXH; ++h) taps[h] = sel(hw, H - 1 - h);
         rows_store_taps<T, NV, WT, MAXH>(p, slot, d0, H, taps);
@@ -465,7 +527,7 @@ __global__ void __launch_bounds__(32 + kMaxRowsD / kVec, 1) dynconv_fwd_rows_ker
       }
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive(empty0 + 8 * s);
+    if (lane == 0) mbar_arrive(empty0 + 8 * cur_s);
   }
 }
 
