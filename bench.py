@@ -54,12 +54,16 @@ def peaks():
     return FALLBACK_HBM_GBS, "fallback"
 
 
-def dram_traffic():
-    """Per-launch DRAM bytes of the kernels from a committed ncu summary."""
+def dram_traffic(channels=4096, train_seqs=8):
+    """Per-launch DRAM bytes of the kernels from a committed ncu summary
+    (captured at 4096 channels and 8 x 4096 training tokens), scaled to the
+    channels and training tokens of this run (traffic is proportional to both)."""
     p = ROOT / "profiles" / "dram_traffic.json"
-    if p.exists():
-        return json.loads(p.read_text())
-    return {}
+    if not p.exists():
+        return {}
+    d = {k: v for k, v in json.loads(p.read_text()).items() if not k.startswith("_")}
+    scale = channels / 4096
+    return {k: round(v * scale * (train_seqs / 8 if k.startswith("train") else 1)) for k, v in d.items()}
 
 
 # ---------------------------------------------------------------------------
@@ -557,7 +561,7 @@ def main():
     from greta_plugin_b200 import vllm_conv as vc
 
     peak, peak_kind = peaks()
-    traffic = dram_traffic()
+    traffic = dram_traffic(args.channels, args.train_seqs)
     out = {}
     with ClockSampler(dev.index) as clocks:
         if args.workload in ("prefill", "all"):
