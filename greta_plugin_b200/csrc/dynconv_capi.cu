@@ -138,21 +138,37 @@ cudaError_t run_rows(int dtype, const RowsParams& p, int norm, int gv, dim3 grid
   }
 }
 
-// Launch the row-streaming TMA forward when it applies: rows of at most 4096
-// channels in whole 256-channel blocks, 16-byte aligned tensors, filter rows
-// of whole 16-byte units, DS / SD state, at most kMaxSeqsTma sequences, and
-// room for at least two token rows in flight. Returns -1 when it does not.
+// Channels per CTA of a row-streaming kernel: the widest multiple of 256 that
+// divides D and is at most max_c (0 when there is none).
+int64_t slice_channels(int64_t D, int64_t max_c) {
+  for (int64_t n = 1; n <= D / 256; ++n)
+    if (D % n == 0 && (D / n) % 256 == 0 && D / n <= max_c) return D / n;
+  return 0;
+}
+
+// Launch the row-streaming TMA forward when it applies: rows of whole
+// 256-channel blocks (split over CTAs of at most fwd_rows_max_channels),
+// 16-byte aligned tensors and copies, DS / SD state, at most kMaxSeqsTma
+// sequences, and room for at least two token rows in flight. Returns -1 when
+// it does not.
 int try_rows_fwd(int dtype, RowsParams p, bool gate, int norm, void* stream) {
   if (!g_tma_enabled) return -1;
   const int es = esize(dtype);
   const int64_t D = p.D, W = p.W, G = p.G, DC = D / G;
-  if (D % 256 != 0 || D > kMaxRowsD || W > kMaxWGeneric) return -1;
+  if (D % 256 != 0 || W > kMaxWGeneric) return -1;
   if (p.mode == kModePacked && p.nseq > kMaxSeqsTma) return -1;
   if (p.state != nullptr && p.st_layout != kStDS && p.st_layout != kStSD) return -1;
   for (const void* q : {p.x, p.w, p.g, (const void*)p.y, (const void*)p.yr})
     if (!aligned(q, 16)) return -1;
-  const int64_t rowx = D * es, roww = W * DC * es;
-  if (roww % 16 != 0) return -1;
+  // the W template launch_fwd_rows picks: 4, 7, -8 or -kMaxWGeneric
+  const int wt = W == 4 ? 4 : (W == 7 ? 7 : (W <= 8 ? -8 : -kMaxWGeneric));
+  const int64_t dcta = slice_channels(D, fwd_rows_max_channels(wt));
+  if (dcta == 0) return -1;
+  const int64_t nsplit = D / dcta;
+  if ((W * DC * es) % 16 != 0) return -1;
+  const bool wsplit = nsplit > 1 && W * DC * es > 2048;
+  if (wsplit && ((dcta / G) * es) % 16 != 0) return -1;
+  const int64_t rowx = dcta * es, roww = wsplit ? W * (dcta / G) * es : W * DC * es;
   const bool packed = p.mode == kModePacked;
   const size_t off_stage = packed ? a128((size_t)(p.nseq + 1) * 8) : 0;
   const size_t budget = 200 * 1024;
@@ -184,13 +200,97 @@ int try_rows_fwd(int dtype, RowsParams p, bool gate, int norm, void* stream) {
   p.stage_bytes = (int)stage;
   p.so_w = (int)so_w;
   p.so_g = (int)so_g;
-  const long long work = p.U;
-  long long grid = num_sms();
-  if (work < grid) grid = work;
-  if (grid <= 0) return GRETA_OK;
+  p.dcta = (int)dcta;
+  p.nsplit = (int)nsplit;
+  p.wsplit = wsplit ? 1 : 0;
+  long long ranges = num_sms() / nsplit;
+  if (ranges < 1) ranges = 1;
+  if (p.U < ranges) ranges = p.U;
+  if (ranges <= 0) return GRETA_OK;
   const size_t smem = off_stage + S * stage;
-  return finish(run_rows(dtype, p, norm, group_vec(kVec, G), dim3((unsigned)grid), dim3((unsigned)(32 + D / kVec)),
-                         smem, stream));
+  return finish(run_rows(dtype, p, norm, group_vec(kVec, G), dim3((unsigned)(ranges * nsplit)),
+                         dim3((unsigned)(32 + dcta / kVec)), smem, stream));
+}
+
+cudaError_t run_bwd_rows(int dtype, const BwdRowsParams& p, int norm, int gv, dim3 grid, dim3 block, size_t smem,
+                         void* stream) {
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case GRETA_DT_F32: return launch_bwd_rows_f32(p, norm, gv, grid, block, smem, st);
+    case GRETA_DT_F16: return launch_bwd_rows_f16(p, norm, gv, grid, block, smem, st);
+    default: return launch_bwd_rows_bf16(p, norm, gv, grid, block, smem, st);
+  }
+}
+
+// Launch the row-streaming TMA backward when it applies: rows of whole
+// 256-channel blocks (split over CTAs of at most bwd_rows_max_channels),
+// W <= kMaxWBwdRows, 16-byte aligned tensors and copies, at most kMaxSeqsTma
+// sequences, and room for two stages of token rows (x, filters, dout, gate,
+// saved pre-norm output). Returns -1 when it does not.
+int try_rows_bwd(int dtype, BwdRowsParams p, int norm, void* stream) {
+  if (!g_tma_enabled) return -1;
+  const int es = esize(dtype);
+  const int64_t D = p.D, W = p.W, G = p.G, DC = D / G;
+  if (D % 256 != 0 || W > kMaxWBwdRows) return -1;
+  if (p.mode == kModePacked && p.nseq > kMaxSeqsTma) return -1;
+  for (const void* q : {p.x, p.w, p.g, p.yr, p.dout, (const void*)p.dx, (const void*)p.dw, (const void*)p.dg})
+    if (!aligned(q, 16)) return -1;
+  // the W template launch_bwd_rows picks: 4, 7 or -kMaxWBwdRows
+  const int wt = W == 4 ? 4 : (W == 7 ? 7 : -kMaxWBwdRows);
+  const int64_t dcta = slice_channels(D, bwd_rows_max_channels(wt));
+  if (dcta == 0) return -1;
+  const int64_t nsplit = D / dcta;
+  if ((W * DC * es) % 16 != 0) return -1;
+  // split filter rows per tap when whole rows would be re-read by many CTAs
+  const bool wsplit = nsplit > 1 && W * DC * es > 2048;
+  if (wsplit && ((dcta / G) * es) % 16 != 0) return -1;
+  const int64_t rowx = dcta * es, roww = wsplit ? W * (dcta / G) * es : W * DC * es;
+  const bool gate = p.g != nullptr, has_yr = norm != GRETA_NORM_NONE;
+  const bool packed = p.mode == kModePacked;
+  const size_t off_stage = packed ? a128((size_t)(p.nseq + 1) * 8) : 0;
+  const size_t budget = 200 * 1024;
+  if (off_stage >= budget) return -1;
+  const int64_t per_token = 2 * rowx + roww + (gate ? rowx : 0) + (has_yr ? rowx : 0);
+  const int64_t inflight = (int64_t)(budget - off_stage) / per_token;
+  if (inflight < 2) return -1;
+  int S, BT;
+  if (inflight >= 8) {
+    S = 4;
+    BT = (int)(inflight / 4 < 16 ? inflight / 4 : 16);
+  } else {
+    S = (int)(inflight < kMaxStages ? inflight : kMaxStages);
+    BT = 1;
+  }
+  size_t so_w, so_do, so_g, so_yr, stage;
+  for (;;) {
+    so_w = a128((size_t)BT * rowx);
+    so_do = so_w + a128((size_t)BT * roww);
+    so_g = so_do + a128((size_t)BT * rowx);
+    so_yr = so_g + (gate ? a128((size_t)BT * rowx) : 0);
+    stage = so_yr + (has_yr ? a128((size_t)BT * rowx) : 0);
+    if (off_stage + S * stage <= budget || (BT == 1 && S == 2)) break;
+    if (BT > 1) --BT; else --S;
+  }
+  if (off_stage + S * stage > budget) return -1;
+  p.BT = BT;
+  p.stages = S;
+  p.off_bnd = 0;
+  p.off_stage = (int)off_stage;
+  p.stage_bytes = (int)stage;
+  p.so_w = (int)so_w;
+  p.so_do = (int)so_do;
+  p.so_g = (int)so_g;
+  p.so_yr = (int)so_yr;
+  p.dcta = (int)dcta;
+  p.nsplit = (int)nsplit;
+  p.wsplit = wsplit ? 1 : 0;
+  long long ranges = num_sms() / nsplit;
+  if (ranges < 1) ranges = 1;
+  if (p.T < ranges) ranges = p.T;
+  if (ranges <= 0) return GRETA_OK;
+  const size_t smem = off_stage + S * stage;
+  return finish(run_bwd_rows(dtype, p, norm, group_vec(kVec, G), dim3((unsigned)(ranges * nsplit)),
+                             dim3((unsigned)(32 + dcta / kVec)), smem, stream));
 }
 
 // A run must cover the W-1 history positions: a request's old slot taps are
@@ -256,6 +356,18 @@ int greta_dynconv_bwd(int dtype, const void* x, const void* w, const void* gate,
   int nv = pick_nv(dtype, D, G, {x, gate, yr, dout, dx, dg}, w);
   if (nv == kVec && !aligned(dw, (int64_t)group_vec(kVec, G) * esize(dtype))) nv = G > 32 ? 0 : 1;
   if (nv == 0) return GRETA_ERR_ALIGNMENT;
+  if (nv == kVec) {
+    BwdRowsParams tp{};
+    tp.x = x; tp.w = w; tp.g = gate; tp.yr = norm != GRETA_NORM_NONE ? yr : nullptr; tp.dout = dout;
+    tp.dx = dx; tp.dw = dw; tp.dg = dg;
+    tp.starts = cu_seqlens; tp.starts_i64 = cu_seqlens_int64 ? 1 : 0;
+    tp.mode = cu_seqlens ? kModePacked : kModeSingle;
+    tp.nseq = cu_seqlens ? num_seqs : 1;
+    tp.T = T; tp.D = (int)D; tp.W = (int)W; tp.G = (int)G;
+    tp.eps = eps;
+    const int r = try_rows_bwd(dtype, tp, norm, stream);
+    if (r >= 0) return r;
+  }
   const Shape sh = shape_for(GRETA_PATH_BWD, (int)W - 1);
   BwdParams p{};
   p.x = x; p.w = w; p.g = gate; p.yr = norm != GRETA_NORM_NONE ? yr : nullptr; p.dout = dout;
@@ -399,9 +511,15 @@ int greta_dynconv_set_tma(int enable) {
 }
 
 int greta_dynconv_device_errors(int clear) {
-  const int a = device_errors_f32(clear != 0), b = device_errors_f16(clear != 0), c = device_errors_bf16(clear != 0);
-  if (a < 0 || b < 0 || c < 0) return -1;
-  return a | b | c;
+  const bool cl = clear != 0;
+  const int v[6] = {device_errors_f32(cl),           device_errors_f16(cl),           device_errors_bf16(cl),
+                    device_errors_bwd_rows_f32(cl), device_errors_bwd_rows_f16(cl), device_errors_bwd_rows_bf16(cl)};
+  int all = 0;
+  for (int e : v) {
+    if (e < 0) return -1;
+    all |= e;
+  }
+  return all;
 }
 
 int greta_dynconv_set_launch_shape(int path, int block_x, int block_y, int tokens) {

@@ -2,11 +2,13 @@
 // forward, HF inference from context, vLLM chunked prefill): row streaming
 // through the Tensor Memory Accelerator.
 //
-// Each persistent CTA (one per SM) owns a contiguous range of tokens and ALL
-// D channels. Its producer warp streams the range in stages of BT whole token
-// rows -- x rows, filter rows and gate rows are contiguous in memory, so a
-// stage is a few large cp.async.bulk copies (kilobytes each), completion
-// counted on the stage's "full" mbarrier. Its D/8 consumer threads each own
+// Each persistent CTA (one per SM) owns a contiguous range of tokens and a
+// slice of dcta channels: all D channels when D fits one CTA
+// (fwd_rows_max_channels), else the channels are split over nsplit CTAs that
+// stream the same range. Its producer warp streams the range in stages of BT
+// token rows -- x rows, filter rows and gate rows are contiguous in memory, so
+// a stage is a few large cp.async.bulk copies (kilobytes each), completion
+// counted on the stage's "full" mbarrier. Its dcta/8 consumer threads each own
 // 8 channels for the whole range: they keep the last W-1 inputs in registers
 // across stages, read the token's operands from shared memory, compute the
 // fp32 conv + group norm + gate and store y directly. Consumer warps arrive on
@@ -28,18 +30,9 @@
 // kErrTimeout in the device error word and returns.
 #pragma once
 
-#include "dynconv_common.cuh"
+#include "dynconv_tma_common.cuh"
 
 namespace greta {
-
-constexpr int kMaxStages = 8;
-constexpr int kMaxSeqsTma = 2048;   // sequence offsets held in shared memory
-constexpr int kMaxRowsD = 4096;     // widest row (D / 8 consumer threads <= 512)
-constexpr int kErrTimeout = 2;      // device error bit: an mbarrier wait gave up
-
-// Device error word of this translation unit (one per element type); read
-// and cleared on the host through greta_dynconv_device_errors.
-static __device__ int g_tma_errors = 0;
 
 struct RowsParams {
   const void* x;
@@ -54,6 +47,9 @@ struct RowsParams {
   long long T;     // tokens (SINGLE / PACKED) or Q (CONTEXT)
   long long U;     // tokens of the launch (T, or nseq * Q for CONTEXT)
   int D, W, G;
+  int dcta;    // channels per CTA (a multiple of 256 dividing D)
+  int nsplit;  // D / dcta: CTAs per token range
+  int wsplit;  // 1: stage only the CTA's filters (per tap), 0: whole filter rows
   int BT;      // token rows per stage
   int stages;  // ring depth (<= kMaxStages)
   // cache-slot state (PACKED only)
@@ -69,59 +65,8 @@ struct RowsParams {
 };
 
 // ---------------------------------------------------------------------------
-// mbarrier and bulk-copy primitives (PTX)
-// ---------------------------------------------------------------------------
-__device__ __forceinline__ void mbar_init(unsigned bar, unsigned count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive_expect_tx(unsigned bar, unsigned bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes) : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive(unsigned bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(bar) : "memory");
-}
-
-// Bounded wait for the phase with the given parity; false on timeout (~1 s).
-__device__ __forceinline__ bool mbar_wait(unsigned bar, unsigned parity) {
-  for (unsigned it = 0; it < (1u << 24); ++it) {
-    unsigned done;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(done)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    if (done) return true;
-    if (it > 64) __nanosleep(64);
-  }
-  return false;
-}
-
-// global -> shared bulk copy; bytes a multiple of 16, both addresses 16-byte aligned
-__device__ __forceinline__ void bulk_g2s(unsigned dst, const void* src, unsigned bytes, unsigned bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(dst),
-      "l"(src), "r"(bytes), "r"(bar)
-      : "memory");
-}
-
-// ---------------------------------------------------------------------------
 // ranges
 // ---------------------------------------------------------------------------
-// last s in [0, n) with bnd[s] <= v (bnd non-decreasing, bnd[0] <= v)
-__device__ __forceinline__ long long seq_of(const long long* bnd, long long n, long long v) {
-  long long lo = 0, hi = n - 1;
-  while (lo < hi) {
-    const long long mid = (lo + hi + 1) >> 1;
-    if (bnd[mid] <= v)
-      lo = mid;
-    else
-      hi = mid - 1;
-  }
-  return lo;
-}
-
 // Move a range boundary out of the first W-1 tokens of a request. The
 // requests cover tokens [ulo, uhi).
 __device__ __forceinline__ long long adjust_boundary(const RowsParams& p, const long long* bnd, long long v, int H,
@@ -213,7 +158,8 @@ __device__ __forceinline__ void rows_store_taps(const RowsParams& p, long long s
 // the kernel
 // ---------------------------------------------------------------------------
 template <typename T, int WT, int NORM, int GV>
-__global__ void __launch_bounds__(32 + kMaxRowsD / kVec, 1) dynconv_fwd_rows_kernel(const RowsParams p) {
+__global__ void __launch_bounds__(32 + fwd_rows_max_channels(WT) / kVec, 1)
+    dynconv_fwd_rows_kernel(const RowsParams p) {
   constexpr int NV = kVec;
   constexpr int MAXW = WT > 0 ? WT : -WT;
   constexpr int MAXH = MAXW > 1 ? MAXW - 1 : 1;
@@ -243,34 +189,36 @@ __global__ void __launch_bounds__(32 + kMaxRowsD / kVec, 1) dynconv_fwd_rows_ker
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
   if (p.mode == kModePacked)
-    for (long long i = threadIdx.x; i <= p.nseq; i += blockDim.x)
-      bnd[i] = clampll(load_idx(p.starts, i, p.starts_i64), 0, p.T);
-  __syncthreads();
-  if (p.mode == kModePacked && threadIdx.x == 0) {
-    // make the offsets non-decreasing (a decreasing offset = an empty request)
-    for (long long i = 1; i <= p.nseq; ++i)
-      if (bnd[i] < bnd[i - 1]) bnd[i] = bnd[i - 1];
-  }
-  __syncthreads();
+    load_offsets(bnd, p.starts, p.starts_i64, p.nseq, p.T);
+  else
+    __syncthreads();
 
-  // this CTA's token range inside the covered tokens [ulo, uhi)
+  // this CTA's channel slice [c0, c0 + dcta) and token range inside the
+  // covered tokens [ulo, uhi)
+  const int range = (int)blockIdx.x / p.nsplit, nranges = (int)gridDim.x / p.nsplit;
+  const int c0 = ((int)blockIdx.x % p.nsplit) * p.dcta;
   const long long ulo = p.mode == kModePacked ? bnd[0] : 0;
   const long long uhi = p.mode == kModePacked ? bnd[p.nseq] : p.U;
-  const long long nominal = (uhi - ulo + gridDim.x - 1) / gridDim.x;
-  const long long u0 = adjust_boundary(p, bnd, ulo + (long long)blockIdx.x * nominal, H, uhi);
-  const long long u1 = adjust_boundary(p, bnd, ulo + (long long)(blockIdx.x + 1) * nominal, H, uhi);
+  const long long nominal = (uhi - ulo + nranges - 1) / nranges;
+  const long long u0 = adjust_boundary(p, bnd, ulo + (long long)range * nominal, H, uhi);
+  const long long u1 = adjust_boundary(p, bnd, ulo + (long long)(range + 1) * nominal, H, uhi);
   const long long ntiles = u1 > u0 ? (u1 - u0 + p.BT - 1) / p.BT : 0;
 
   const T* __restrict__ xg = reinterpret_cast<const T*>(p.x);
   const T* __restrict__ wg = reinterpret_cast<const T*>(p.w);
   const T* __restrict__ gg = reinterpret_cast<const T*>(p.g);
   const long long xrow_b = p.mode == kModeContext ? p.T + H : 0;  // context rows per batch row
+  // staged row sizes (bytes): a channel slice of x / gate, and the filters
+  // (the slice's per tap, or whole rows)
+  const int fct = p.dcta / G;  // filters of the slice
+  const unsigned rowx = (unsigned)(p.dcta * ES);
+  const unsigned roww = p.wsplit ? (unsigned)(W * fct * ES) : (unsigned)(W * DC * ES);
 
   if (warp == 0) {
     // =========================== producer ===========================
     if (lane != 0) return;
-    const unsigned rowx = (unsigned)(D * ES), roww = (unsigned)(W * DC * ES);
     const unsigned sb0 = smem_addr(smem + p.off_stage);
+    const bool whole = p.nsplit == 1;  // slices are whole rows
     int s = 0;
     unsigned par = 0;  // parity of the stage's current use
     long long t0 = u0;
@@ -290,20 +238,40 @@ __global__ void __launch_bounds__(32 + kMaxRowsD / kVec, 1) dynconv_fwd_rows_ker
       if (p.mode == kModeContext) {
         for (int j = 0; j < n; ++j) {
           const long long u = t0 + j, b = u / p.T, q = u % p.T;
-          bulk_g2s(sb + j * rowx, xg + (b * xrow_b + H + q) * D, rowx, bar);
+          bulk_g2s(sb + j * rowx, xg + (b * xrow_b + H + q) * D + c0, rowx, bar);
         }
-      } else {
+      } else if (whole) {
         bulk_g2s(sb, xg + t0 * D, (unsigned)n * rowx, bar);
+      } else {
+        for (int j = 0; j < n; ++j) bulk_g2s(sb + j * rowx, xg + (t0 + j) * D + c0, rowx, bar);
       }
-      bulk_g2s(sb + p.so_w, wg + t0 * W * DC, (unsigned)n * roww, bar);
-      if (gg != nullptr) bulk_g2s(sb + p.so_g, gg + t0 * D, (unsigned)n * rowx, bar);
+      if (p.wsplit) {
+        const unsigned tapb = (unsigned)(fct * ES);
+        for (int j = 0; j < n; ++j)
+          for (int k = 0; k < W; ++k)
+            bulk_g2s(sb + p.so_w + j * roww + k * tapb, wg + ((t0 + j) * W + k) * DC + c0 / G, tapb, bar);
+      } else {
+        bulk_g2s(sb + p.so_w, wg + t0 * W * DC, (unsigned)n * roww, bar);
+      }
+      if (gg != nullptr) {
+        if (whole) {
+          bulk_g2s(sb + p.so_g, gg + t0 * D, (unsigned)n * rowx, bar);
+        } else {
+          for (int j = 0; j < n; ++j) bulk_g2s(sb + p.so_g + j * rowx, gg + (t0 + j) * D + c0, rowx, bar);
+        }
+      }
     }
     return;
   }
 
   // =========================== consumers ===========================
-  const int d0 = ((int)threadIdx.x - 32) * NV;
-  const long long f0 = d0 / G;
+  const int cidx = (int)threadIdx.x - 32;
+  const int d0 = c0 + cidx * NV;  // first channel of this thread
+  // this thread's operands in a stage: channel offset in the slice rows, and
+  // filter offset / tap stride (elements) in the staged filter rows
+  const int xoff = cidx * NV * ES;
+  const int woff = (p.wsplit ? (d0 - c0) / G : d0 / G) * ES;
+  const int wtap = p.wsplit ? fct : (int)DC;
   const int lpg = (GV == 1 && G > NV) ? G / NV : 1;
   T* __restrict__ yg = reinterpret_cast<T*>(p.y);
   T* __restrict__ yrg = reinterpret_cast<T*>(p.yr);
@@ -311,7 +279,7 @@ __global__ void __launch_bounds__(32 + kMaxRowsD / kVec, 1) dynconv_fwd_rows_ker
 
   // empty requests, dealt round-robin: a slot without history is cleared
   if (has_state)
-    for (long long s = blockIdx.x; s < p.nseq; s += gridDim.x)
+    for (long long s = range; s < p.nseq; s += nranges)
       if (bnd[s + 1] == bnd[s]) {
         long long sl = p.slots[s];
         if (sl >= p.num_slots) {
@@ -406,10 +374,9 @@ __global__ void __launch_bounds__(32 + kMaxRowsD / kVec, 1) dynconv_fwd_rows_ker
   };
   sync_window();
 
-  const int rowx = D * ES, roww = W * DC * ES;
   int koff[MAXW];  // byte offset of the filter of the input k steps back
 #pragma unroll
-  for (int k = 0; k < MAXW; ++k) koff[k] = (k < W ? (W - 1 - k) : 0) * (int)DC * ES;
+  for (int k = 0; k < MAXW; ++k) koff[k] = (k < W ? (W - 1 - k) : 0) * wtap * ES;
   T* yp = yg + u0 * D + d0;
   T* yrp = yrg != nullptr ? yrg + u0 * D + d0 : nullptr;
   int s = 0;
@@ -427,9 +394,9 @@ __global__ void __launch_bounds__(32 + kMaxRowsD / kVec, 1) dynconv_fwd_rows_ker
       par ^= 1u;
     }
     const int n = (int)min((long long)p.BT, u1 - t0);
-    const unsigned char* xsp = stg + d0 * ES;
-    const unsigned char* wsp = stg + p.so_w + f0 * ES;
-    const unsigned char* gsp = stg + p.so_g + d0 * ES;
+    const unsigned char* xsp = stg + xoff;
+    const unsigned char* wsp = stg + p.so_w + woff;
+    const unsigned char* gsp = stg + p.so_g + xoff;
     for (int j = 0; j < n; ++j, xsp += rowx, wsp += roww, gsp += rowx, yp += D) {
       const long long u = t0 + j;
       if (p.mode == kModeContext) {

@@ -5,6 +5,7 @@
 #pragma once
 
 #include "dynconv_bwd.cuh"
+#include "dynconv_bwd_tma.cuh"
 #include "dynconv_fwd.cuh"
 #include "dynconv_fwd_tma.cuh"
 
@@ -156,17 +157,6 @@ cudaError_t launch_fwd_rows(const RowsParams& p, int norm, int gv, dim3 grid, di
   return rows_norm<T, -kMaxWGeneric>(p, norm, gv, grid, block, smem, st);
 }
 
-// Read (and clear) this translation unit's device error word.
-inline int read_device_errors(bool clear) {
-  int v = 0;
-  if (cudaMemcpyFromSymbol(&v, g_tma_errors, sizeof(int)) != cudaSuccess) return -1;
-  if (clear && v != 0) {
-    const int z = 0;
-    cudaMemcpyToSymbol(g_tma_errors, &z, sizeof(int));
-  }
-  return v;
-}
-
 // Entry points defined by the per-dtype translation units.
 cudaError_t launch_fwd_f32(const FwdParams&, int, int, int, const LaunchShape&, cudaStream_t);
 cudaError_t launch_fwd_f16(const FwdParams&, int, int, int, const LaunchShape&, cudaStream_t);
@@ -180,5 +170,12 @@ cudaError_t launch_fwd_rows_bf16(const RowsParams&, int, int, dim3, dim3, size_t
 int device_errors_f32(bool clear);
 int device_errors_f16(bool clear);
 int device_errors_bf16(bool clear);
+// row-streaming backward (dynconv_bwd_rows_<dtype>.cu)
+cudaError_t launch_bwd_rows_f32(const BwdRowsParams&, int, int, dim3, dim3, size_t, cudaStream_t);
+cudaError_t launch_bwd_rows_f16(const BwdRowsParams&, int, int, dim3, dim3, size_t, cudaStream_t);
+cudaError_t launch_bwd_rows_bf16(const BwdRowsParams&, int, int, dim3, dim3, size_t, cudaStream_t);
+int device_errors_bwd_rows_f32(bool clear);
+int device_errors_bwd_rows_f16(bool clear);
+int device_errors_bwd_rows_bf16(bool clear);
 
 }  // namespace greta

@@ -129,3 +129,140 @@ def test_packed_prefill_with_state(capi, layout, W, G):
                            np.array(init), G, 2)
     assert_close(ya, yo, torch.bfloat16)
     assert np.array_equal(sa.float().cpu().numpy(), so)
+
+
+# --------------------------------------------------------------------------
+# channel-split launches (a token range streamed by several CTAs, one per
+# channel slice) and the row-streaming backward
+# --------------------------------------------------------------------------
+@pytest.mark.parametrize("D,W,G,norm,gate_on,dtype", [
+    (4096, 7, 128, True, True, torch.bfloat16),   # 2 slices of 2048, whole filter rows
+    (4096, 7, 1, False, False, torch.bfloat16),   # 2 slices, filters staged per tap
+    (2048, 5, 4, True, True, torch.bfloat16),     # runtime W <= 8: 2 slices of 1024
+    (1024, 12, 8, False, True, torch.float16),    # runtime W <= 16: 2 slices of 512
+    (2048, 3, 16, True, False, torch.float32),
+])
+def test_forward_channel_split(capi, D, W, G, norm, gate_on, dtype):
+    from greta_plugin_b200.dynamic_conv import dynconv_fwd
+
+    g = torch.Generator().manual_seed(D + W + G)
+    lens = [1, W - 1, 0, 3, 200, 2 * W, 90]
+    T = sum(lens)
+    x = rand(g, 1, T, D, dtype=dtype)
+    w = rand(g, T, W, D // G, scale=0.5, dtype=dtype)
+    gate = rand(g, 1, T, D, dtype=dtype) if gate_on else None
+    cu = ragged_cu(lens)
+    xd, wd, gd, cud = x.to(DEV), w.to(DEV), None if gate is None else gate.to(DEV), cu.to(DEV)
+    (y1, yr1, _, _), (y2, yr2, _, _) = both(
+        capi, lambda: dynconv_fwd(xd, wd, gd, cud, G, norm=norm, save_pre=True))
+    _same((y1, yr1), (y2, yr2))
+    yo, _ = oracle.fwd(to_np(x[0]), to_np(w), to_np(gate[0]) if gate_on else None, cu.numpy(), G, int(norm))
+    assert_close(y1[0], yo, dtype)
+
+
+@pytest.mark.parametrize("layout", ["DS", "SD"])
+def test_packed_prefill_channel_split(capi, layout):
+    """W = 7, G = 128 at 4096 channels: two CTAs per token range, each reading
+    and writing its half of every slot."""
+    from greta_plugin_b200 import packed_dynamic_conv_triton
+
+    W, G, D, n_slots = 7, 128, 4096, 10
+    g = torch.Generator().manual_seed(77)
+    lens = [1, 3, 6, 7, 150, 0, 40, 9]
+    slots = [3, -1, 7, 0, 8, 5, 2, 9]
+    init = [1, 1, 0, 1, 1, 0, 1, 1]
+    T = sum(lens)
+    x = rand(g, T, D).to(DEV)
+    w = rand(g, T, W, D // G, scale=0.5).to(DEV)
+    gate = rand(g, T, D).to(DEV)
+    logical = rand(g, n_slots, D, W - 1)
+    starts = torch.tensor([0] + list(np.cumsum(lens)), dtype=torch.int32, device=DEV)
+    sl = torch.tensor(slots, dtype=torch.int32, device=DEV)
+    ini = torch.tensor(init, dtype=torch.int8, device=DEV)
+
+    def make_state():
+        if layout == "DS":
+            return logical.to(DEV).contiguous()
+        return logical.transpose(1, 2).contiguous().to(DEV).transpose(1, 2)
+
+    sa, sb = make_state(), make_state()
+    capi.set_tma(True)
+    ya = packed_dynamic_conv_triton(x, w, gate, sa, starts, sl, ini, G)
+    capi.set_tma(False)
+    yb = packed_dynamic_conv_triton(x, w, gate, sb, starts, sl, ini, G)
+    capi.set_tma(True)
+    torch.cuda.synchronize()
+    assert torch.equal(ya, yb)
+    assert torch.equal(sa, sb)
+    yo, so = oracle.packed(to_np(x), to_np(w), to_np(gate), to_np(logical), starts.cpu().numpy(), np.array(slots),
+                           np.array(init), G, 2)
+    assert_close(ya, yo, torch.bfloat16)
+    assert np.array_equal(sa.float().cpu().numpy(), so)
+
+
+def test_inference_channel_split(capi):
+    from greta_plugin_b200 import dynamic_causal_conv1d_inference
+
+    W, G, D, B, Q = 7, 128, 2048, 2, 300
+    g = torch.Generator().manual_seed(5)
+    ctx = rand(g, B, Q + W - 1, D).to(DEV)
+    w = rand(g, B, Q, W, D // G, scale=0.5).to(DEV)
+    gate = rand(g, B, Q, D).to(DEV)
+    a, b = both(capi, lambda: dynamic_causal_conv1d_inference(ctx, w, gate, G, True))
+    _same(a, b)
+    yo = oracle.inference(to_np(ctx), to_np(w), to_np(gate), G, 1)
+    assert_close(a, yo, torch.bfloat16)
+
+
+@pytest.mark.parametrize("D,W,G,norm,gate_on,dtype,lens", [
+    (512, 4, 1, False, False, torch.bfloat16, [1, 2, 3, 300, 0, 64, 5]),
+    (512, 4, 64, True, True, torch.bfloat16, [1, 2, 3, 300, 0, 64, 5]),
+    (4096, 4, 1, False, False, torch.bfloat16, [700, 3, 1, 300]),      # 2 slices, filters per tap
+    (4096, 4, 1, True, True, torch.bfloat16, [257, 2, 400]),
+    (2048, 7, 128, True, True, torch.bfloat16, [1, 6, 7, 8, 500, 0]),  # 2 slices of 1024, whole rows
+    (1024, 7, 16, False, True, torch.float16, [30, 31, 200]),
+    (768, 3, 2, True, False, torch.float32, [5, 100, 1, 2]),           # 768 = 3 x 256: one slice
+    (1024, 2, 4, False, True, torch.bfloat16, [1, 1, 1, 1, 90]),
+    (512, 8, 8, True, True, torch.bfloat16, [9, 8, 7, 150]),
+    (256, 5, 128, True, True, torch.bfloat16, [4, 5, 6, 60]),
+    (512, 4, 1, True, False, torch.bfloat16, [1, 2, 3]),                # fewer tokens than SMs
+])
+def test_training_backward(capi, D, W, G, norm, gate_on, dtype, lens):
+    """Row-streaming backward against the register-staged backward (bit for
+    bit) and the oracle, over ragged packs with empty and short sequences."""
+    from greta_plugin_b200.dynamic_conv import dynconv_bwd, dynconv_fwd
+
+    g = torch.Generator().manual_seed(D * 3 + W * 5 + G)
+    T = sum(lens)
+    x = rand(g, 1, T, D, dtype=dtype)
+    w = rand(g, T, W, D // G, scale=(1.0 / W) ** 0.5, dtype=dtype)
+    gate = rand(g, 1, T, D, dtype=dtype) if gate_on else None
+    dout = rand(g, 1, T, D, dtype=dtype)
+    cu = ragged_cu(lens)
+    xd, wd, dd, cud = x.to(DEV), w.to(DEV), dout.to(DEV), cu.to(DEV)
+    gd = gate.to(DEV) if gate_on else None
+    _, yr, _, _ = dynconv_fwd(xd, wd, gd, cud, G, norm=norm, save_pre=True)
+    a, b = both(capi, lambda: dynconv_bwd(xd, wd, gd, yr, dd, cud, G, norm, 1e-6, 64, None))
+    _same(a, b)
+    dx, dw, dg = a
+    gn = to_np(gate[0]) if gate_on else None
+    dxo, dwo, dgo = oracle.bwd(to_np(x[0]), to_np(w), gn, to_np(dout[0]), cu.numpy(), G, int(norm),
+                               yr=to_np(yr[0]) if norm else None)
+    assert_close(dx[0], dxo, dtype)
+    assert_close(dw, dwo, dtype)
+    if gate_on:
+        assert_close(dg[0], dgo, dtype)
+
+
+def test_training_backward_single_sequence(capi):
+    from greta_plugin_b200.dynamic_conv import dynconv_bwd
+
+    g = torch.Generator().manual_seed(11)
+    T, D, W = 1000, 4096, 4
+    x, w = rand(g, 1, T, D).to(DEV), rand(g, T, W, D, scale=0.5).to(DEV)
+    dout = rand(g, 1, T, D).to(DEV)
+    a, b = both(capi, lambda: dynconv_bwd(x, w, None, None, dout, None, 1, False, 1e-6, 64, None))
+    _same(a, b)
+    dxo, dwo, _ = oracle.bwd(to_np(x[0]), to_np(w), None, to_np(dout[0]), None, 1, 0)
+    assert_close(a[0][0], dxo, torch.bfloat16)
+    assert_close(a[1], dwo, torch.bfloat16)
