@@ -158,6 +158,7 @@ int try_rows_fwd(int dtype, RowsParams p, bool gate, int norm, void* stream) {
   if (D % 256 != 0 || W > kMaxWGeneric) return -1;
   if (p.mode == kModePacked && p.nseq > kMaxSeqsTma) return -1;
   if (p.state != nullptr && p.st_layout != kStDS && p.st_layout != kStSD) return -1;
+  if (p.U >= ((int64_t)1 << 31)) return -1;  // token positions are 32-bit inside the kernel
   for (const void* q : {p.x, p.w, p.g, (const void*)p.y, (const void*)p.yr})
     if (!aligned(q, 16)) return -1;
   // the W template launch_fwd_rows picks: 4, 7, -8 or -kMaxWGeneric
@@ -170,7 +171,10 @@ int try_rows_fwd(int dtype, RowsParams p, bool gate, int norm, void* stream) {
   if (wsplit && ((dcta / G) * es) % 16 != 0) return -1;
   const int64_t rowx = dcta * es, roww = wsplit ? W * (dcta / G) * es : W * DC * es;
   const bool packed = p.mode == kModePacked;
-  const size_t off_stage = packed ? a128((size_t)(p.nseq + 1) * 8) : 0;
+  // offsets [nseq + 1] x 8 B, then (with a state) slots [nseq] x 4 B and flags [nseq] x 1 B
+  const size_t off_meta = packed ? (size_t)(p.nseq + 1) * 8 : 0;
+  const size_t meta = packed && p.state != nullptr ? (size_t)p.nseq * 5 : 0;
+  const size_t off_stage = packed ? a128(off_meta + meta) : 0;
   const size_t budget = 200 * 1024;
   if (off_stage >= budget) return -1;
   const int64_t per_token = rowx + roww + (gate ? rowx : 0);
@@ -196,6 +200,7 @@ int try_rows_fwd(int dtype, RowsParams p, bool gate, int norm, void* stream) {
   p.BT = BT;
   p.stages = S;
   p.off_bnd = 0;
+  p.off_meta = (int)off_meta;
   p.off_stage = (int)off_stage;
   p.stage_bytes = (int)stage;
   p.so_w = (int)so_w;
@@ -203,10 +208,19 @@ int try_rows_fwd(int dtype, RowsParams p, bool gate, int norm, void* stream) {
   p.dcta = (int)dcta;
   p.nsplit = (int)nsplit;
   p.wsplit = wsplit ? 1 : 0;
+  p.log2g = 0;
+  while ((1 << p.log2g) < G) ++p.log2g;
   long long ranges = num_sms() / nsplit;
   if (ranges < 1) ranges = 1;
   if (p.U < ranges) ranges = p.U;
   if (ranges <= 0) return GRETA_OK;
+  p.nominal = (p.U + ranges - 1) / ranges;
+  // L2 prefetch at the start: the first rows of every range, about 48 MB in
+  // all (a whole short prefill; the head of each range of a long stream)
+  const int64_t full_row = D * es * (gate ? 2 : 1) + W * DC * es;
+  int64_t pf = ((int64_t)48 << 20) / (ranges * full_row);
+  if (pf > p.nominal) pf = p.nominal;
+  p.pf_rows = (int)(pf < 1 ? 1 : pf);
   const size_t smem = off_stage + S * stage;
   return finish(run_rows(dtype, p, norm, group_vec(kVec, G), dim3((unsigned)(ranges * nsplit)),
                          dim3((unsigned)(32 + dcta / kVec)), smem, stream));

@@ -236,10 +236,14 @@ struct SeqHit {
   int init;
 };
 
+//
+// With skip = 1 only the chunks after each sequence's first are numbered
+// (chunk j >= 1 of sequence i is number j - 1 + the count of earlier
+// sequences' later chunks); the first chunks are then addressed directly.
 template <int kItems>
 __device__ bool block_find_chunk(const void* starts, int is64, long long nseq, long long T,
                                  int chunk, long long cid, const int* slots,
-                                 const signed char* initial, SeqHit& hit) {
+                                 const signed char* initial, SeqHit& hit, int skip = 0) {
   __shared__ long long sh_warp[32];
   __shared__ SeqHit sh_hit;
   __shared__ int sh_found;
@@ -266,6 +270,7 @@ __device__ bool block_find_chunk(const void* starts, int is64, long long nseq, l
         n = bnd[k + 1] - bnd[k];
         if (n < 0) n = 0;
         n = n > 0 ? (n + chunk - 1) / chunk : 1;
+        n -= skip;
       }
       cnt[k] = n;
       tot += n;
@@ -296,7 +301,7 @@ __device__ bool block_find_chunk(const void* starts, int is64, long long nseq, l
       if (i0 + k < nseq && cid >= ex && cid < ex + cnt[k]) {
         SeqHit h;
         h.s = i0 + k;
-        h.j = cid - ex;
+        h.j = cid - ex + skip;
         h.a = bnd[k];
         h.b = bnd[k + 1] < bnd[k] ? bnd[k] : bnd[k + 1];
         h.slot_raw = slots ? slots[i0 + k] : -1;

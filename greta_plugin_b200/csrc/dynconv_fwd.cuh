@@ -64,10 +64,22 @@ __device__ __forceinline__ bool resolve_fwd_chunk(const FwdParams& p, ChunkInfo&
     ci.has_state = 1;
     return true;
   }
-  // PACKED
+  // PACKED: CTA row cid < nseq is the first chunk of request cid (its offsets,
+  // slot and flag are independent loads: no search); the rows after them are
+  // the requests' later chunks, found by a block-wide scan.
   SeqHit h;
-  if (!block_find_chunk<4>(p.starts, p.starts_i64, p.nseq, p.T, p.chunk, cid, p.slots, p.initial, h))
+  if (cid < p.nseq) {
+    h.s = cid;
+    h.j = 0;
+    h.a = clampll(load_idx(p.starts, cid, p.starts_i64), 0, p.T);
+    h.b = clampll(load_idx(p.starts, cid + 1, p.starts_i64), 0, p.T);
+    if (h.b < h.a) h.b = h.a;
+    h.slot_raw = p.slots != nullptr ? p.slots[cid] : -1;
+    h.init = p.initial != nullptr ? (int)p.initial[cid] : 0;
+  } else if (!block_find_chunk<4>(p.starts, p.starts_i64, p.nseq, p.T, p.chunk, cid - p.nseq, p.slots, p.initial,
+                                  h, 1)) {
     return false;
+  }
   ci.len = h.b - h.a;
   ci.x_base = h.a;
   ci.o_base = h.a;

@@ -47,6 +47,9 @@ struct RowsParams {
   long long T;     // tokens (SINGLE / PACKED) or Q (CONTEXT)
   long long U;     // tokens of the launch (T, or nseq * Q for CONTEXT)
   int D, W, G;
+  int log2g;          // G = 1 << log2g
+  long long nominal;  // tokens per range before boundary moves: ceil(U / ranges)
+  int pf_rows;        // rows of the range prefetched into L2 at the start (>= 1)
   int dcta;    // channels per CTA (a multiple of 256 dividing D)
   int nsplit;  // D / dcta: CTAs per token range
   int wsplit;  // 1: stage only the CTA's filters (per tap), 0: whole filter rows
@@ -60,8 +63,10 @@ struct RowsParams {
   const signed char* initial;
   int* err;  // slot-range error bits (may be null)
   float eps;
-  // shared-memory layout (bytes from the dynamic base)
-  int off_bnd, off_stage, stage_bytes, so_w, so_g;
+  // shared-memory layout (bytes from the dynamic base): sequence offsets
+  // [nseq + 1] (int64), request slots [nseq] (int32) and flags [nseq] (int8),
+  // then the stages
+  int off_bnd, off_meta, off_stage, stage_bytes, so_w, so_g;
 };
 
 // ---------------------------------------------------------------------------
@@ -171,7 +176,7 @@ __global__ void __launch_bounds__(32 + fwd_rows_max_channels(WT) / kVec, 1)
   const int H = W - 1;
   const int D = p.D;
   const int G = p.G;
-  const long long DC = D / G;
+  const long long DC = D >> p.log2g;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nconsw = (int)(blockDim.x >> 5) - 1;  // consumer warps
   const int S = p.stages;
@@ -181,6 +186,12 @@ __global__ void __launch_bounds__(32 + fwd_rows_max_channels(WT) / kVec, 1)
   const unsigned full0 = smem_addr(&bars[0]), empty0 = smem_addr(&bars[kMaxStages]);
   long long* bnd = reinterpret_cast<long long*>(smem + p.off_bnd);
 
+  const int range = (int)blockIdx.x / p.nsplit, nranges = (int)gridDim.x / p.nsplit;
+  const int c0 = ((int)blockIdx.x % p.nsplit) * p.dcta;
+  const bool has_state = p.state != nullptr;
+  int* sslot = reinterpret_cast<int*>(smem + p.off_meta);  // per-request slot and initial flag (PACKED + state)
+  signed char* sinit = reinterpret_cast<signed char*>(smem + p.off_meta + 4 * p.nseq);
+
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(full0 + 8 * s, 1);
@@ -188,21 +199,53 @@ __global__ void __launch_bounds__(32 + fwd_rows_max_channels(WT) / kVec, 1)
     }
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
-  if (p.mode == kModePacked)
-    load_offsets(bnd, p.starts, p.starts_i64, p.nseq, p.T);
-  else
+  if (warp == 0 && lane >= 8 && lane < 12 && p.mode != kModeContext) {
+    // Start HBM on this CTA's rows before anything else: bulk L2 prefetch of
+    // the first pf_rows rows of its nominal range (the range when the
+    // requests cover all tokens; boundary moves shift it by < W-1 rows), and
+    // a touch of its first output row. The staged copies then hit L2, so the
+    // stage ring refills at L2 latency while HBM streams continuously.
+    const long long u = min((long long)range * p.nominal, p.U - 1);
+    const unsigned n = (unsigned)min((long long)p.pf_rows, p.U - u);
+    const T* xs = reinterpret_cast<const T*>(p.x) + u * D;
+    const T* gs = p.g != nullptr ? reinterpret_cast<const T*>(p.g) + u * D : nullptr;
+    if (lane == 8 || (lane == 10 && gs != nullptr)) {
+      const T* base = lane == 8 ? xs : gs;
+      if (p.nsplit == 1) {
+        bulk_prefetch_l2(base, n * (unsigned)(D * ES));
+      } else {
+        for (unsigned j = 0; j < n; ++j) bulk_prefetch_l2(base + (long long)j * D + c0, (unsigned)(p.dcta * ES));
+      }
+    } else if (lane == 9) {
+      bulk_prefetch_l2(reinterpret_cast<const T*>(p.w) + u * W * DC, n * (unsigned)(W * DC * ES));
+    } else if (lane == 11) {
+      asm volatile("prefetch.global.L2 [%0];\n" ::"l"(reinterpret_cast<const T*>(p.y) + u * D + c0));
+    }
+  }
+  if (p.mode == kModePacked) {
+    // sequence offsets, and with a state the requests' slots and flags, all
+    // loaded at once (the slots do not depend on the offsets)
+    for (long long i = threadIdx.x; i <= p.nseq; i += blockDim.x) {
+      bnd[i] = clampll(load_idx(p.starts, i, p.starts_i64), 0, p.T);
+      if (has_state && i < p.nseq) {
+        sslot[i] = p.slots[i];
+        sinit[i] = p.initial[i];
+      }
+    }
     __syncthreads();
+    if (threadIdx.x == 0)
+      for (long long i = 1; i <= p.nseq; ++i)
+        if (bnd[i] < bnd[i - 1]) bnd[i] = bnd[i - 1];
+  }
+  __syncthreads();
 
   // this CTA's channel slice [c0, c0 + dcta) and token range inside the
-  // covered tokens [ulo, uhi)
-  const int range = (int)blockIdx.x / p.nsplit, nranges = (int)gridDim.x / p.nsplit;
-  const int c0 = ((int)blockIdx.x % p.nsplit) * p.dcta;
+  // covered tokens [ulo, uhi): nominal ranges of p.nominal = ceil(U / ranges)
+  // tokens (set on the host: no division here)
   const long long ulo = p.mode == kModePacked ? bnd[0] : 0;
   const long long uhi = p.mode == kModePacked ? bnd[p.nseq] : p.U;
-  const long long nominal = (uhi - ulo + nranges - 1) / nranges;
-  const long long u0 = adjust_boundary(p, bnd, ulo + (long long)range * nominal, H, uhi);
-  const long long u1 = adjust_boundary(p, bnd, ulo + (long long)(range + 1) * nominal, H, uhi);
-  const long long ntiles = u1 > u0 ? (u1 - u0 + p.BT - 1) / p.BT : 0;
+  const long long u0 = adjust_boundary(p, bnd, ulo + (long long)range * p.nominal, H, uhi);
+  const long long u1 = adjust_boundary(p, bnd, ulo + (long long)(range + 1) * p.nominal, H, uhi);
 
   const T* __restrict__ xg = reinterpret_cast<const T*>(p.x);
   const T* __restrict__ wg = reinterpret_cast<const T*>(p.w);
@@ -210,9 +253,12 @@ __global__ void __launch_bounds__(32 + fwd_rows_max_channels(WT) / kVec, 1)
   const long long xrow_b = p.mode == kModeContext ? p.T + H : 0;  // context rows per batch row
   // staged row sizes (bytes): a channel slice of x / gate, and the filters
   // (the slice's per tap, or whole rows)
-  const int fct = p.dcta / G;  // filters of the slice
+  const int fct = p.dcta >> p.log2g;  // filters of the slice
   const unsigned rowx = (unsigned)(p.dcta * ES);
   const unsigned roww = p.wsplit ? (unsigned)(W * fct * ES) : (unsigned)(W * DC * ES);
+  // CONTEXT: batch row and position of token u0 (token counts fit 32 bits)
+  const int q0 = p.mode == kModeContext ? (int)((unsigned)u0 % (unsigned)p.T) : 0;
+  const long long b0 = p.mode == kModeContext ? (long long)((unsigned)u0 / (unsigned)p.T) : 0;
 
   if (warp == 0) {
     // =========================== producer ===========================
@@ -221,8 +267,10 @@ __global__ void __launch_bounds__(32 + fwd_rows_max_channels(WT) / kVec, 1)
     const bool whole = p.nsplit == 1;  // slices are whole rows
     int s = 0;
     unsigned par = 0;  // parity of the stage's current use
-    long long t0 = u0;
-    for (long long i = 0; i < ntiles; ++i, t0 += p.BT) {
+    long long cb = b0;  // CONTEXT: batch row and position of the next token
+    int cq = q0;
+    int i = 0;
+    for (long long t0 = u0; t0 < u1; t0 += p.BT, ++i) {
       if (i >= S && !mbar_wait(empty0 + 8 * s, par ^ 1u)) {
         atomicOr(&g_tma_errors, kErrTimeout);
         return;
@@ -237,8 +285,11 @@ __global__ void __launch_bounds__(32 + fwd_rows_max_channels(WT) / kVec, 1)
       mbar_arrive_expect_tx(bar, (unsigned)n * (rowx + roww + (gg != nullptr ? rowx : 0u)));
       if (p.mode == kModeContext) {
         for (int j = 0; j < n; ++j) {
-          const long long u = t0 + j, b = u / p.T, q = u % p.T;
-          bulk_g2s(sb + j * rowx, xg + (b * xrow_b + H + q) * D + c0, rowx, bar);
+          bulk_g2s(sb + j * rowx, xg + (cb * xrow_b + H + cq) * D + c0, rowx, bar);
+          if (++cq == (int)p.T) {
+            cq = 0;
+            ++cb;
+          }
         }
       } else if (whole) {
         bulk_g2s(sb, xg + t0 * D, (unsigned)n * rowx, bar);
@@ -247,9 +298,10 @@ __global__ void __launch_bounds__(32 + fwd_rows_max_channels(WT) / kVec, 1)
       }
       if (p.wsplit) {
         const unsigned tapb = (unsigned)(fct * ES);
+        const long long fc0 = c0 >> p.log2g;
         for (int j = 0; j < n; ++j)
           for (int k = 0; k < W; ++k)
-            bulk_g2s(sb + p.so_w + j * roww + k * tapb, wg + ((t0 + j) * W + k) * DC + c0 / G, tapb, bar);
+            bulk_g2s(sb + p.so_w + j * roww + k * tapb, wg + ((t0 + j) * W + k) * DC + fc0, tapb, bar);
       } else {
         bulk_g2s(sb + p.so_w, wg + t0 * W * DC, (unsigned)n * roww, bar);
       }
@@ -270,23 +322,22 @@ __global__ void __launch_bounds__(32 + fwd_rows_max_channels(WT) / kVec, 1)
   // this thread's operands in a stage: channel offset in the slice rows, and
   // filter offset / tap stride (elements) in the staged filter rows
   const int xoff = cidx * NV * ES;
-  const int woff = (p.wsplit ? (d0 - c0) / G : d0 / G) * ES;
+  const int woff = (p.wsplit ? (d0 - c0) >> p.log2g : d0 >> p.log2g) * ES;
   const int wtap = p.wsplit ? fct : (int)DC;
   const int lpg = (GV == 1 && G > NV) ? G / NV : 1;
   T* __restrict__ yg = reinterpret_cast<T*>(p.y);
   T* __restrict__ yrg = reinterpret_cast<T*>(p.yr);
-  const bool has_state = p.state != nullptr;
 
   // empty requests, dealt round-robin: a slot without history is cleared
   if (has_state)
     for (long long s = range; s < p.nseq; s += nranges)
       if (bnd[s + 1] == bnd[s]) {
-        long long sl = p.slots[s];
+        long long sl = sslot[s];
         if (sl >= p.num_slots) {
           if (p.err != nullptr && d0 == 0) atomicOr(p.err, 1);
           sl = -1;
         }
-        if (sl >= 0 && p.initial[s] == 0) {
+        if (sl >= 0 && sinit[s] == 0) {
           PX z[MAXH];
 #pragma unroll
           for (int h = 0; h < MAXH; ++h) zero(z[h]);
@@ -317,13 +368,13 @@ __global__ void __launch_bounds__(32 + fwd_rows_max_channels(WT) / kVec, 1)
 #pragma unroll
     for (int i = 0; i < MAXH; ++i) zero(hw[i]);
     if (!has_state) return;
-    long long sl = p.slots[sq];
+    long long sl = sslot[sq];
     if (sl >= p.num_slots) {
       if (p.err != nullptr && d0 == 0) atomicOr(p.err, 1);
       sl = -1;
     }
     slot = sl < 0 ? -1 : sl;
-    if (slot >= 0 && p.initial[sq] != 0) rows_old_taps<T, NV, WT, MAXH>(p, slot, d0, H, hw);
+    if (slot >= 0 && sinit[sq] != 0) rows_old_taps<T, NV, WT, MAXH>(p, slot, d0, H, hw);
     if (slot >= 0 && rb > u1) {
       // the request continues past this CTA: its new taps are its last W-1
       // inputs (it has more than W-1 tokens), written now, after the old
@@ -341,10 +392,9 @@ __global__ void __launch_bounds__(32 + fwd_rows_max_channels(WT) / kVec, 1)
 
   if (u0 < u1) {
     if (p.mode == kModeContext) {
-      const long long b = u0 / p.T, q = u0 % p.T;
 #pragma unroll
       for (int i = 0; i < MAXH; ++i)
-        if (i < H) hw[i] = ld<T, NV>(xg + (b * xrow_b + H + q - 1 - i) * D + d0);
+        if (i < H) hw[i] = ld<T, NV>(xg + (b0 * xrow_b + H + q0 - 1 - i) * D + d0);
     } else {
       find_request(u0);
       if (u0 == ra) {
@@ -381,8 +431,9 @@ __global__ void __launch_bounds__(32 + fwd_rows_max_channels(WT) / kVec, 1)
   T* yrp = yrg != nullptr ? yrg + u0 * D + d0 : nullptr;
   int s = 0;
   unsigned par = 0;
-  long long t0 = u0;
-  for (long long i = 0; i < ntiles; ++i, t0 += p.BT) {
+  long long cb = b0;  // CONTEXT: batch row and position of the current token
+  int cq = q0;
+  for (long long t0 = u0; t0 < u1; t0 += p.BT) {
     if (!mbar_wait(full0 + 8 * s, par)) {
       if (lane == 0) atomicOr(&g_tma_errors, kErrTimeout);
       return;
@@ -400,12 +451,15 @@ __global__ void __launch_bounds__(32 + fwd_rows_max_channels(WT) / kVec, 1)
     for (int j = 0; j < n; ++j, xsp += rowx, wsp += roww, gsp += rowx, yp += D) {
       const long long u = t0 + j;
       if (p.mode == kModeContext) {
-        if (u != u0 && u % p.T == 0) {  // a new batch row: its history is its context
-          const long long b = u / p.T;
+        if (u != u0 && cq == 0) {  // a new batch row: its history is its context
 #pragma unroll
           for (int k = 0; k < MAXH; ++k)
-            if (k < H) hw[k] = ld<T, NV>(xg + (b * xrow_b + H - 1 - k) * D + d0);
+            if (k < H) hw[k] = ld<T, NV>(xg + (cb * xrow_b + H - 1 - k) * D + d0);
           sync_window();
+        }
+        if (++cq == (int)p.T) {  // position of the next token
+          cq = 0;
+          ++cb;
         }
       } else if (u >= rb) {
         find_request(u);  // skips empty requests

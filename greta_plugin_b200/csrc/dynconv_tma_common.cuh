@@ -68,6 +68,18 @@ __device__ __forceinline__ bool mbar_wait(unsigned bar, unsigned parity) {
   return false;
 }
 
+// Bulk prefetch of [src, src + bytes) into L2, in pieces of at most 256 KB;
+// bytes a multiple of 16, src 16-byte aligned. Completion is not tracked.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, unsigned bytes) {
+  const char* a = static_cast<const char*>(src);
+  while (bytes > 0) {
+    const unsigned n = bytes < (256u << 10) ? bytes : (256u << 10);
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(a), "r"(n) : "memory");
+    a += n;
+    bytes -= n;
+  }
+}
+
 // global -> shared bulk copy; bytes a multiple of 16, both addresses 16-byte aligned
 __device__ __forceinline__ void bulk_g2s(unsigned dst, const void* src, unsigned bytes, unsigned bar) {
   asm volatile(
