@@ -91,6 +91,21 @@ __device__ __forceinline__ float to_f(float v) { return v; }
 __device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
 __device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
 
+// a * b + c with a, b in the I/O type and c in fp32, one rounding. For 16-bit
+// types this is sm_100's mixed-precision FMA (the operands widen exactly), so
+// the result equals fmaf(to_f(a), to_f(b), c) without the two conversions.
+__device__ __forceinline__ float fma_io(float a, float b, float c) { return fmaf(a, b, c); }
+__device__ __forceinline__ float fma_io(__nv_bfloat16 a, __nv_bfloat16 b, float c) {
+  float r;
+  asm("fma.rn.f32.bf16 %0, %1, %2, %3;" : "=f"(r) : "h"(__bfloat16_as_ushort(a)), "h"(__bfloat16_as_ushort(b)), "f"(c));
+  return r;
+}
+__device__ __forceinline__ float fma_io(__half a, __half b, float c) {
+  float r;
+  asm("fma.rn.f32.f16 %0, %1, %2, %3;" : "=f"(r) : "h"(__half_as_ushort(a)), "h"(__half_as_ushort(b)), "f"(c));
+  return r;
+}
+
 template <typename T>
 __device__ __forceinline__ T from_f(float v);
 template <>

@@ -408,22 +408,9 @@ __global__ void __launch_bounds__(32 + fwd_rows_max_channels(WT) / kVec, 1)
     }
   }
 
-  // History window in registers. For W <= 4 it is kept as fp32 (each input is
-  // converted once); wider windows stay in the I/O type. The fp32 copy of a
-  // bf16 / fp16 / fp32 input converts back exactly, so the slot write-back
-  // remains a bit copy.
-  constexpr bool kFloatWin = MAXH <= 3;
-  float hf[kFloatWin ? MAXH : 1][NV];
-  auto sync_window = [&]() {
-    if constexpr (kFloatWin) {
-#pragma unroll
-      for (int k = 0; k < MAXH; ++k)
-#pragma unroll
-        for (int c = 0; c < NV; ++c) hf[k][c] = to_f(hw[k].v[c]);
-    }
-  };
-  sync_window();
-
+  // The history window stays in the I/O type: the taps multiply with
+  // fma_io (for 16-bit types sm_100's mixed-precision FMA), so no input or
+  // filter element is converted, and the slot write-back is a bit copy.
   int koff[MAXW];  // byte offset of the filter of the input k steps back
 #pragma unroll
   for (int k = 0; k < MAXW; ++k) koff[k] = (k < W ? (W - 1 - k) : 0) * wtap * ES;
@@ -455,7 +442,6 @@ __global__ void __launch_bounds__(32 + fwd_rows_max_channels(WT) / kVec, 1)
 #pragma unroll
           for (int k = 0; k < MAXH; ++k)
             if (k < H) hw[k] = ld<T, NV>(xg + (cb * xrow_b + H - 1 - k) * D + d0);
-          sync_window();
         }
         if (++cq == (int)p.T) {  // position of the next token
           cq = 0;
@@ -464,7 +450,6 @@ __global__ void __launch_bounds__(32 + fwd_rows_max_channels(WT) / kVec, 1)
       } else if (u >= rb) {
         find_request(u);  // skips empty requests
         begin_request();
-        sync_window();
       }
       const PX xc = *reinterpret_cast<const PX*>(xsp);
       PW wc[MAXW];
@@ -473,26 +458,15 @@ __global__ void __launch_bounds__(32 + fwd_rows_max_channels(WT) / kVec, 1)
         zero(wc[k]);
         if (k < W) wc[k] = *reinterpret_cast<const PW*>(wsp + koff[k]);
       }
-      float xf[NV];
-#pragma unroll
-      for (int c = 0; c < NV; ++c) xf[c] = to_f(xc.v[c]);
       float acc[NV];
 #pragma unroll
       for (int c = 0; c < NV; ++c) acc[c] = 0.f;
 #pragma unroll
       for (int k = MAXW - 1; k >= 0; --k) {
         if (k < W) {
+          const PX& xs = (k == 0) ? xc : hw[k > 0 ? k - 1 : 0];
 #pragma unroll
-          for (int c = 0; c < NV; ++c) {
-            float xv;
-            if (k == 0)
-              xv = xf[c];
-            else if constexpr (kFloatWin)
-              xv = hf[k > 0 ? k - 1 : 0][c];
-            else
-              xv = to_f(hw[k > 0 ? k - 1 : 0].v[c]);
-            acc[c] = fmaf(xv, to_f(wc[k].v[c / GC]), acc[c]);
-          }
+          for (int c = 0; c < NV; ++c) acc[c] = fma_io(xs.v[c], wc[k].v[c / GC], acc[c]);
         }
       }
       if (NORM != kNormNone) {
@@ -519,28 +493,13 @@ __global__ void __launch_bounds__(32 + fwd_rows_max_channels(WT) / kVec, 1)
         for (int c = 0; c < NV; ++c) o.v[c] = from_f<T>(acc[c]);
         st<T, NV>(yp, o);
       }
-      if constexpr (kFloatWin) {
 #pragma unroll
-        for (int k = MAXH - 1; k > 0; --k)
-#pragma unroll
-          for (int c = 0; c < NV; ++c) hf[k][c] = hf[k - 1][c];
-#pragma unroll
-        for (int c = 0; c < NV; ++c) hf[0][c] = xf[c];
-      } else {
-#pragma unroll
-        for (int k = MAXH - 1; k > 0; --k) hw[k] = hw[k - 1];
-        hw[0] = xc;
-      }
+      for (int k = MAXH - 1; k > 0; --k) hw[k] = hw[k - 1];
+      hw[0] = xc;
       if (has_state && head_here && slot >= 0 && u == rb - 1) {
         // the request ends here: the window holds the input at rb-1-k (old
         // taps for positions before ra), so the new tap h is window[H-1-h]
         PX taps[MAXH];
-        if constexpr (kFloatWin) {
-#pragma unroll
-          for (int k = 0; k < MAXH; ++k)
-#pragma unroll
-            for (int c = 0; c < NV; ++c) hw[k].v[c] = from_f<T>(hf[k][c]);
-        }
 #pragma unroll
         for (int h = 0; h < MAXH; ++h) taps[h] = sel(hw, H - 1 - h);
         rows_store_taps<T, NV, WT, MAXH>(p, slot, d0, H, taps);
