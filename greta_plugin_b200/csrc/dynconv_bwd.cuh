@@ -170,8 +170,8 @@ __global__ void __launch_bounds__(256) dynconv_bwd_kernel(const BwdParams p) {
 #pragma unroll
           for (int c = 0; c < NV; ++c) {
             const float xv = to_f(xs.v[c]);
-            prod[c] = dy[c] * xv;
-            if (NORM == kNormNone && gg != nullptr) yc[c] = fmaf(xv, to_f(wr[i].v[c / GC]), yc[c]);
+            prod[c] = __fmul_rn(dy[c], xv);  // not fused into the group sum below
+            if (NORM == kNormNone && gg != nullptr) yc[c] = fma_io(xs.v[c], wr[i].v[c / GC], yc[c]);
           }
           group_sum<NV, GV>(prod, s, lpg);
           if (dw_writer) {
@@ -199,7 +199,7 @@ __global__ void __launch_bounds__(256) dynconv_bwd_kernel(const BwdParams p) {
     float done[NV];
     if (H == 0) {
 #pragma unroll
-      for (int c = 0; c < NV; ++c) done[c] = dy[c] * to_f(wr[0].v[c / GC]);
+      for (int c = 0; c < NV; ++c) done[c] = __fmul_rn(dy[c], to_f(wr[0].v[c / GC]));
     } else {
 #pragma unroll
       for (int j = 0; j < MAXH; ++j)
@@ -220,7 +220,7 @@ __global__ void __launch_bounds__(256) dynconv_bwd_kernel(const BwdParams p) {
 #pragma unroll
         for (int c = 0; c < NV; ++c) pend[j][c] = pend[j - 1][c];
 #pragma unroll
-      for (int c = 0; c < NV; ++c) pend[0][c] = dy[c] * to_f(wr[0].v[c / GC]);
+      for (int c = 0; c < NV; ++c) pend[0][c] = __fmul_rn(dy[c], to_f(wr[0].v[c / GC]));
     }
     const long long tc = t - H;
     if (tc >= rs && tc < re && active) {

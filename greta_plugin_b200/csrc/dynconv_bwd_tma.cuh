@@ -335,10 +335,11 @@ __global__ void __launch_bounds__(32 + bwd_rows_max_channels(WT) / kVec, 1)
             const PX& xs = (i == 0) ? xr : hw[i > 0 ? i - 1 : 0];
             float prod[NV], sm[GV];
 #pragma unroll
-            for (int c = 0; c < NV; ++c) {
-              const float xv = to_f(xs.v[c]);
-              prod[c] = dy[c] * xv;
-              if (NORM == kNormNone && gg != nullptr) yc[c] = fmaf(xv, to_f(wr[i].v[c / GC]), yc[c]);
+            for (int c = 0; c < NV; c += 2)
+              mul2(prod[c], prod[c + 1], dy[c], dy[c + 1], to_f(xs.v[c]), to_f(xs.v[c + 1]));
+            if (NORM == kNormNone && gg != nullptr) {
+#pragma unroll
+              for (int c = 0; c < NV; ++c) yc[c] = fma_io(xs.v[c], wr[i].v[c / GC], yc[c]);
             }
             group_sum<NV, GV>(prod, sm, lpg);
             if (dw_writer) {
@@ -366,14 +367,16 @@ __global__ void __launch_bounds__(32 + bwd_rows_max_channels(WT) / kVec, 1)
       float done[NV];
       if (H == 0) {
 #pragma unroll
-        for (int c = 0; c < NV; ++c) done[c] = dy[c] * to_f(wr[0].v[c / GC]);
+        for (int c = 0; c < NV; ++c) done[c] = __fmul_rn(dy[c], to_f(wr[0].v[c / GC]));
       } else {
 #pragma unroll
         for (int q = 0; q < MAXH; ++q)
-          if (q < H)
+          if (q < H) {
+            const PW& wq = wr[q + 1 < MAXW ? q + 1 : 0];
 #pragma unroll
-            for (int c = 0; c < NV; ++c)
-              pend[q][c] = fmaf(dy[c], to_f(wr[q + 1 < MAXW ? q + 1 : 0].v[c / GC]), pend[q][c]);
+            for (int c = 0; c < NV; c += 2)
+              fma2(pend[q][c], pend[q][c + 1], dy[c], dy[c + 1], to_f(wq.v[c / GC]), to_f(wq.v[(c + 1) / GC]));
+          }
 #pragma unroll
         for (int c = 0; c < NV; ++c) {
           float v = pend[0][c];
@@ -387,7 +390,8 @@ __global__ void __launch_bounds__(32 + bwd_rows_max_channels(WT) / kVec, 1)
 #pragma unroll
           for (int c = 0; c < NV; ++c) pend[q][c] = pend[q - 1][c];
 #pragma unroll
-        for (int c = 0; c < NV; ++c) pend[0][c] = dy[c] * to_f(wr[0].v[c / GC]);
+        for (int c = 0; c < NV; c += 2)
+          mul2(pend[0][c], pend[0][c + 1], dy[c], dy[c + 1], to_f(wr[0].v[c / GC]), to_f(wr[0].v[(c + 1) / GC]));
       }
       const long long tc = u - H;
       if (tc >= max(ra, u0) && tc < u1) {

@@ -100,6 +100,29 @@ __device__ __forceinline__ float fma_io(__nv_bfloat16 a, __nv_bfloat16 b, float 
   asm("fma.rn.f32.bf16 %0, %1, %2, %3;" : "=f"(r) : "h"(__bfloat16_as_ushort(a)), "h"(__bfloat16_as_ushort(b)), "f"(c));
   return r;
 }
+// Two fp32 lanes per instruction (sm_100's packed fp32 pipe); each lane is
+// rounded exactly like fmaf / a * b.
+__device__ __forceinline__ unsigned long long pack2(float a, float b) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void unpack2(unsigned long long r, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+// d[c] = a[c] * b[c] + d[c] for c = 0, 1
+__device__ __forceinline__ void fma2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
+  unsigned long long r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(pack2(a0, a1)), "l"(pack2(b0, b1)), "l"(pack2(d0, d1)));
+  unpack2(r, d0, d1);
+}
+// d[c] = a[c] * b[c] for c = 0, 1
+__device__ __forceinline__ void mul2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
+  unsigned long long r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(pack2(a0, a1)), "l"(pack2(b0, b1)));
+  unpack2(r, d0, d1);
+}
+
 __device__ __forceinline__ float fma_io(__half a, __half b, float c) {
   float r;
   asm("fma.rn.f32.f16 %0, %1, %2, %3;" : "=f"(r) : "h"(__half_as_ushort(a)), "h"(__half_as_ushort(b)), "f"(c));

@@ -293,7 +293,7 @@ __global__ void __launch_bounds__(256) dynconv_fwd_kernel(const FwdParams p) {
       if (i < W) {
         const Pack<T, NV>& xs = (i == 0) ? cur.x : hw[i > 0 ? i - 1 : 0];
 #pragma unroll
-        for (int c = 0; c < NV; ++c) acc[c] = fmaf(to_f(xs.v[c]), to_f(cur.w[i].v[c / GC]), acc[c]);
+        for (int c = 0; c < NV; ++c) acc[c] = fma_io(xs.v[c], cur.w[i].v[c / GC], acc[c]);
       }
     }
     const long long orow = (ci.o_base + t) * D + d0;
