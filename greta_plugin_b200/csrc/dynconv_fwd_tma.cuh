@@ -225,19 +225,20 @@ __global__ void __launch_bounds__(32 + fwd_rows_max_channels(WT) / kVec, 1)
   if (p.mode == kModePacked) {
     // sequence offsets, and with a state the requests' slots and flags, all
     // loaded at once (the slots do not depend on the offsets)
+    int dec = 0;  // this thread saw a decreasing offset
     for (long long i = threadIdx.x; i <= p.nseq; i += blockDim.x) {
-      bnd[i] = clampll(load_idx(p.starts, i, p.starts_i64), 0, p.T);
+      const long long v = clampll(load_idx(p.starts, i, p.starts_i64), 0, p.T);
+      bnd[i] = v;
+      if (i > 0 && v < clampll(load_idx(p.starts, i - 1, p.starts_i64), 0, p.T)) dec = 1;
       if (has_state && i < p.nseq) {
         sslot[i] = p.slots[i];
         sinit[i] = p.initial[i];
       }
     }
+    monotone_offsets(bnd, p.nseq, __syncthreads_or(dec));
+  } else {
     __syncthreads();
-    if (threadIdx.x == 0)
-      for (long long i = 1; i <= p.nseq; ++i)
-        if (bnd[i] < bnd[i - 1]) bnd[i] = bnd[i - 1];
   }
-  __syncthreads();
 
   // this CTA's channel slice [c0, c0 + dcta) and token range inside the
   // covered tokens [ulo, uhi): nominal ranges of p.nominal = ceil(U / ranges)

@@ -104,17 +104,29 @@ __device__ __forceinline__ long long seq_of(const long long* bnd, long long n, l
   return lo;
 }
 
+// Make the offsets in shared memory non-decreasing (a decreasing offset is an
+// empty request) when some thread saw a decrease; all threads call this after
+// the barrier that published the offsets, and it ends with one when it works.
+__device__ __forceinline__ void monotone_offsets(long long* bnd, long long nseq, int any_decrease) {
+  if (!any_decrease) return;  // uniform: the barrier's reduction
+  if (threadIdx.x == 0)
+    for (long long i = 1; i <= nseq; ++i)
+      if (bnd[i] < bnd[i - 1]) bnd[i] = bnd[i - 1];
+  __syncthreads();
+}
+
 // Load the sequence offsets into shared memory (clamped to [0, T]) and make
 // them non-decreasing: a decreasing offset is an empty request. Ends with a
 // CTA barrier.
 __device__ __forceinline__ void load_offsets(long long* bnd, const void* starts, int is64, long long nseq,
                                              long long T) {
-  for (long long i = threadIdx.x; i <= nseq; i += blockDim.x) bnd[i] = clampll(load_idx(starts, i, is64), 0, T);
-  __syncthreads();
-  if (threadIdx.x == 0)
-    for (long long i = 1; i <= nseq; ++i)
-      if (bnd[i] < bnd[i - 1]) bnd[i] = bnd[i - 1];
-  __syncthreads();
+  int dec = 0;  // this thread saw a decreasing offset
+  for (long long i = threadIdx.x; i <= nseq; i += blockDim.x) {
+    const long long v = clampll(load_idx(starts, i, is64), 0, T);
+    bnd[i] = v;
+    if (i > 0 && v < clampll(load_idx(starts, i - 1, is64), 0, T)) dec = 1;
+  }
+  monotone_offsets(bnd, nseq, __syncthreads_or(dec));
 }
 
 }  // namespace greta
