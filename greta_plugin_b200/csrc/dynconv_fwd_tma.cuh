@@ -192,6 +192,21 @@ __global__ void __launch_bounds__(32 + fwd_rows_max_channels(WT) / kVec, 1)
   int* sslot = reinterpret_cast<int*>(smem + p.off_meta);  // per-request slot and initial flag (PACKED + state)
   signed char* sinit = reinterpret_cast<signed char*>(smem + p.off_meta + 4 * p.nseq);
 
+  // Speculative history: when the requests start at token 0, the range most
+  // likely starts at its nominal boundary u_spec inside a request, whose W-1
+  // previous input rows a consumer thread needs first. They are loaded here,
+  // before the sequence offsets arrive, and used if the guess was right.
+  const long long u_spec = (long long)range * p.nominal;
+  Pack<T, kVec> hspec[MAXH];
+#pragma unroll
+  for (int i = 0; i < MAXH; ++i) zero(hspec[i]);
+  if (threadIdx.x >= 32 && p.mode != kModeContext && u_spec >= H && u_spec <= p.U) {
+    const T* xs = reinterpret_cast<const T*>(p.x) + c0 + ((int)threadIdx.x - 32) * kVec;
+#pragma unroll
+    for (int i = 0; i < MAXH; ++i)
+      if (i < H) hspec[i] = ld<T, kVec>(xs + (u_spec - 1 - i) * D);
+  }
+
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(full0 + 8 * s, 1);
@@ -400,6 +415,11 @@ __global__ void __launch_bounds__(32 + fwd_rows_max_channels(WT) / kVec, 1)
       find_request(u0);
       if (u0 == ra) {
         begin_request();
+      } else if (u0 == u_spec) {
+        // mid-request start at the nominal boundary: the rows loaded before
+        // the prologue barrier are the history
+#pragma unroll
+        for (int i = 0; i < MAXH; ++i) hw[i] = hspec[i];
       } else {
         // mid-request start: the boundary rule guarantees u0 - ra >= W-1
 #pragma unroll
