@@ -1,14 +1,16 @@
 """Benchmark of the B200 dynamic causal depthwise convolution.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
-                    [--workload prefill|decode|train|all] [--shard requests|channels]
+                    [--workload prefill|decode|train|greta|all] [--shard requests|channels]
 
 One JSON line on rank 0. The headline (`value`) is the varlen chunked prefill
 with cache-slot state: 8 sequences with lengths ~U[32, 256] packed to <= 1024
 tokens, C = 4096, K = 4, G = 1, bf16, state [64 slots, 4096, 3] read from 8
 distinct random slots and written back. The decode step (256 one-token
 requests, 1024 slots, 10% padding slots) and the training forward + backward
-(8 x 4096 packed tokens, C = 4096, K = 4) are reported under "workloads".
+(8 x 4096 packed tokens, C = 4096, K = 4) are reported under "workloads", with
+the same three paths at Greta's own layer shape (C = 2048, K = 7, G = 128,
+norm and gate on) under "greta_layer".
 
 Timing: W untimed warm-up steps, then exactly K steps between CUDA events on
 the launching stream, bracketed by a barrier and torch.cuda.synchronize();
@@ -331,6 +333,94 @@ def run_train(torch, dev, args, dist, rank, world, peak, traffic):
                 traffic={"fwd": traffic.get("train_fwd"), "bwd": traffic.get("train_bwd")})
 
 
+def run_greta(torch, vc, dev, args, dist, rank, world, peak):
+    """Greta's own layer shape (configuration defaults: hidden 2048, kernel 7,
+    128-channel filter groups, RMS norm and SiLU gate on), informational next to
+    the headline shapes: vLLM prefill (the headline's 8 request lengths) and
+    decode (256 requests) with cache-slot state and the overflow-safe norm, and
+    the training forward (saving the pre-norm output) + backward on 8 x 4096
+    tokens with the plain norm."""
+    from greta_plugin_b200 import _capi
+
+    D, W, G = 2048 // (world if args.shard == "channels" else 1), 7, 128
+    wb = 2 * W * (D // G)  # filter bytes per token
+    seed = 5000 + (rank if args.shard == "requests" else 0)
+
+    def add_gate(b, s):
+        b["gate"] = torch.randn(b["T"], D, device=dev, generator=torch.Generator(device=dev).manual_seed(s)).bfloat16()
+        return b
+
+    def call(b):
+        return vc.packed_dynamic_conv_triton(b["x"], b["w"], b["gate"], b["state"], b["starts"], b["slots"],
+                                             b["init"], G, norm=True, eps=1e-6, out=b["y"])
+
+    out = {"channels": D, "kernel_size": W, "group_size": G, "norm": True, "gate": True}
+    # prefill: x, gate, y per token, filters, old + new slot taps per request
+    probe = add_gate(make_prefill(torch, dev, seed, D=D, W=W, G=G), seed)
+    nb = probe["T"] * (6 * D + wb) + probe["N"] * 4 * (W - 1) * D
+    sets = [probe] + [add_gate(make_prefill(torch, dev, seed + 97 * i, D=D, W=W, G=G), seed + 97 * i)
+                      for i in range(1, n_sets(nb + probe["state"].numel() * 2))]
+    sec = time_graph(torch, sets, call, args.steps, args.warmup, dist) / args.steps
+    out["prefill"] = dict(tokens=probe["T"], us=sec * 1e6, tokens_per_s=probe["T"] / sec, bytes=nb,
+                          frac=nb / sec / 1e9 / peak)
+    del sets, probe
+    # decode: the same bytes per live request; padding rows skip the slot
+    probe = add_gate(make_decode(torch, dev, seed + 1, D=D, W=W, G=G), seed + 1)
+    live = probe["T"] - probe["n_pad"]
+    nb = probe["T"] * (6 * D + wb) + live * 4 * (W - 1) * D
+    sets = [probe] + [add_gate(make_decode(torch, dev, seed + 1 + 31 * i, D=D, W=W, G=G), seed + 1 + 31 * i)
+                      for i in range(1, n_sets(nb + probe["state"].numel() * 2))]
+    sec = time_graph(torch, sets, call, args.decode_steps, args.warmup, dist) / args.decode_steps
+    out["decode"] = dict(tokens=probe["T"], us=sec * 1e6, tokens_per_s=probe["T"] / sec, bytes=nb,
+                         frac=nb / sec / 1e9 / peak)
+    del sets, probe
+    # training
+    S, L = args.train_seqs, 4096
+    T = S * L
+    gd = torch.Generator(device=dev).manual_seed(seed + 2)
+    x = torch.randn(T, D, device=dev, generator=gd).bfloat16()
+    g = torch.randn(T, D, device=dev, generator=gd).bfloat16()
+    w = (torch.randn(T, W, D // G, device=dev, generator=gd) * (1.0 / W) ** 0.5).bfloat16()
+    dout = torch.randn(T, D, device=dev, generator=gd).bfloat16()
+    y, yr, dx, dg, dw = (torch.empty_like(x), torch.empty_like(x), torch.empty_like(x), torch.empty_like(x),
+                         torch.empty_like(w))
+    cu = torch.arange(0, T + 1, L, dtype=torch.int32, device=dev)
+    lib, P, sp, stream = _capi.lib(), _capi.ptr, _capi.stream_of(x), torch.cuda.current_stream()
+
+    def fwd():
+        _capi.check("fwd", lib.greta_dynconv_fwd(_capi.DT_BF16, P(x), P(w), P(g), P(y), P(yr), P(cu), 0, S, T, D, W, G,
+                                                 _capi.NORM_PLAIN, 1e-6, sp))
+
+    def bwd():
+        _capi.check("bwd", lib.greta_dynconv_bwd(_capi.DT_BF16, P(x), P(w), P(g), P(yr), P(dout), P(dx), P(dw), P(dg),
+                                                 P(cu), 0, S, T, D, W, G, _capi.NORM_PLAIN, 1e-6, sp))
+
+    for _ in range(max(args.warmup, 3)):
+        fwd()
+        bwd()
+    torch.cuda.synchronize()
+    barrier(dist)
+    torch.cuda.synchronize()
+    steps = args.train_steps
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3 * steps)]
+    for i in range(steps):
+        ev[3 * i].record(stream)
+        fwd()
+        ev[3 * i + 1].record(stream)
+        bwd()
+        ev[3 * i + 2].record(stream)
+    torch.cuda.synchronize()
+    barrier(dist)
+    f_s = reduce_max(torch, dist, sum(ev[3 * i].elapsed_time(ev[3 * i + 1]) for i in range(steps)) / steps / 1e3)
+    b_s = reduce_max(torch, dist, sum(ev[3 * i + 1].elapsed_time(ev[3 * i + 2]) for i in range(steps)) / steps / 1e3)
+    fb = T * (8 * D + wb)  # x, gate read; y, yr written; filters
+    bb = T * (12 * D + 2 * wb)  # x, gate, yr, dout read; dx, dg written; filters read, dw written
+    out["train"] = dict(tokens=T, fwd_us=f_s * 1e6, bwd_us=b_s * 1e6, fwd_frac=fb / f_s / 1e9 / peak,
+                        bwd_frac=bb / b_s / 1e9 / peak, fwd_bytes=fb, bwd_bytes=bb)
+    out["launches"] = args.steps + args.decode_steps + 2 * steps
+    return out
+
+
 def run_e2e_prefill(torch, vc, dev, args, dist):
     """Public API with host buffers: pinned H2D of the step's inputs, the call,
     D2H of the output -- all inside the timed region."""
@@ -453,7 +543,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--workload", choices=["prefill", "decode", "train", "all"], default="all")
+    ap.add_argument("--workload", choices=["prefill", "decode", "train", "greta", "all"], default="all")
     ap.add_argument("--shard", choices=["requests", "channels"], default="requests")
     ap.add_argument("--decode-steps", type=int, default=None)
     ap.add_argument("--train-steps", type=int, default=None)
@@ -472,8 +562,13 @@ def parse():
     return a
 
 
-def config_block(args, world, prefill):
+def config_block(args, world, prefill, greta=None):
     par = f"{args.shard} x{world}" if world > 1 else "single GPU"
+    if greta is not None:  # --workload greta: the layer-shape prefill leads
+        return {"workload": "varlen chunked prefill with cache-slot state, Greta layer shape (vLLM packed path)",
+                "seqs": 8, "tokens": greta["prefill"]["tokens"], "channels": greta["channels"],
+                "kernel_size": greta["kernel_size"], "group_size": greta["group_size"], "norm": True, "gate": True,
+                "state_slots": 64, "l2": "rotating input sets (> 2x L2)", "parallelism": par}
     return {"workload": "varlen chunked prefill with cache-slot state (vLLM packed path)",
             "seqs": 8, "tokens": prefill["tokens_per_step"] if prefill else None,
             "lengths": prefill.get("lengths") if prefill else None,
@@ -570,6 +665,8 @@ def main():
             out["decode"] = run_decode(torch, vc, dev, args, dist, rank, world, peak, traffic)
         if args.workload in ("train", "all"):
             out["train"] = run_train(torch, dev, args, dist, rank, world, peak, traffic)
+        if args.workload in ("greta", "all"):
+            out["greta_layer"] = run_greta(torch, vc, dev, args, dist, rank, world, peak)
         e2e = run_e2e_prefill(torch, vc, dev, args, dist) if args.workload in ("prefill", "all") else None
     clk = clocks.summary()
 
@@ -585,6 +682,10 @@ def main():
     if rank == 0:
         head = out.get("prefill")
         launches = sum(v.get("launches", 0) for v in out.values()) + (e2e["launches"] if e2e else 0)
+        if head is None and "greta_layer" in out and len(out) == 1:  # --workload greta: its prefill leads
+            gp = out["greta_layer"]["prefill"]
+            head = dict(tokens_per_s=gp["tokens_per_s"], ms_per_step=gp["us"] / 1e3,
+                        achieved_gbs=gp["bytes"] / gp["us"] / 1e3, frac=gp["frac"])
         if head is None:  # a single non-prefill workload was asked for
             key = next(iter(out))
             head = out[key]
@@ -604,7 +705,8 @@ def main():
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic (seeded N(0,1) inputs in the reference layouts)",
-            "config": config_block(args, world, out.get("prefill")),
+            "config": config_block(args, world, out.get("prefill"),
+                                   out["greta_layer"] if set(out) == {"greta_layer"} else None),
             "roofline": {"bound": "hbm", "achieved": head["achieved_gbs"], "peak": peak, "unit": "GB/s",
                          "frac": head["frac"], "traffic": head.get("traffic"),
                          "peak_source": f"{peak_kind} copy bandwidth (MEASURED_PEAKS.json hbm_gbs)"

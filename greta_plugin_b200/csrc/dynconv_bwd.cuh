@@ -145,7 +145,7 @@ __global__ void __launch_bounds__(256) dynconv_bwd_kernel(const BwdParams p) {
         }
         group_sum<NV, GV>(sq, rinv, lpg);
 #pragma unroll
-        for (int gi = 0; gi < GV; ++gi) rinv[gi] = 1.f / sqrtf(rinv[gi] * inv_g + p.eps);
+        for (int gi = 0; gi < GV; ++gi) rinv[gi] = rsqrtf(rinv[gi] * inv_g + p.eps);
 #pragma unroll
         for (int c = 0; c < NV; ++c) sq[c] = to_f(yrr.v[c]) * rinv[c / GC] * dy[c];
         group_sum<NV, GV>(sq, cs, lpg);

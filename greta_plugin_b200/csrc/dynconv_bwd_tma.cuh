@@ -312,7 +312,7 @@ __global__ void __launch_bounds__(32 + bwd_rows_max_channels(WT) / kVec, 1)
         }
         group_sum<NV, GV>(sq, rinv, lpg);
 #pragma unroll
-        for (int gi = 0; gi < GV; ++gi) rinv[gi] = 1.f / sqrtf(rinv[gi] * inv_g + p.eps);
+        for (int gi = 0; gi < GV; ++gi) rinv[gi] = rsqrtf(rinv[gi] * inv_g + p.eps);
 #pragma unroll
         for (int c = 0; c < NV; ++c) sq[c] = to_f(yrr.v[c]) * rinv[c / GC] * dy[c];
         group_sum<NV, GV>(sq, cs, lpg);

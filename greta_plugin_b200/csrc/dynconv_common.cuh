@@ -166,7 +166,9 @@ __device__ __forceinline__ P sel(const P (&a)[N], int idx) {
   return r;
 }
 
-__device__ __forceinline__ float sigmoidf_(float v) { return 1.f / (1.f + __expf(-v)); }
+// 1 / (1 + e^-v) with the fast exponential and reciprocal (a few ulp, like the
+// reference kernels' sigmoid); 0 for very negative v, 1 for very positive v.
+__device__ __forceinline__ float sigmoidf_(float v) { return __fdividef(1.f, 1.f + __expf(-v)); }
 
 // ---------------------------------------------------------------------------
 // group reductions. NV channels per thread; GV groups per thread when G < NV
@@ -206,6 +208,8 @@ __device__ __forceinline__ void group_max(const float (&v)[NV], float (&out)[GV]
 //   plain : y * 1/sqrt(mean(y^2) + eps)               (greta/dynamic_conv.py:251-255)
 //   stable: s = max(max|y|, 1); y / (s * sqrt(mean((y/s)^2) + eps/s^2))
 //                                                    (greta_vllm/triton_conv.py:71-77)
+// The reciprocal square root and the division by s are the hardware's fast
+// forms (rsqrt, reciprocal), as in the reference kernels' tl.rsqrt.
 template <int NORM, int NV, int GV>
 __device__ __forceinline__ void apply_norm(float (&acc)[NV], int G, int lpg, float eps) {
   constexpr int GC = NV / GV;
@@ -216,7 +220,7 @@ __device__ __forceinline__ void apply_norm(float (&acc)[NV], int G, int lpg, flo
     for (int c = 0; c < NV; ++c) sq[c] = acc[c] * acc[c];
     group_sum<NV, GV>(sq, ss, lpg);
 #pragma unroll
-    for (int gi = 0; gi < GV; ++gi) ss[gi] = 1.f / sqrtf(ss[gi] * inv_g + eps);
+    for (int gi = 0; gi < GV; ++gi) ss[gi] = rsqrtf(ss[gi] * inv_g + eps);
 #pragma unroll
     for (int c = 0; c < NV; ++c) acc[c] *= ss[c / GC];
   } else if (NORM == kNormStable) {
@@ -225,19 +229,18 @@ __device__ __forceinline__ void apply_norm(float (&acc)[NV], int G, int lpg, flo
     for (int c = 0; c < NV; ++c) ab[c] = fabsf(acc[c]);
     group_max<NV, GV>(ab, mx, lpg);
 #pragma unroll
-    for (int gi = 0; gi < GV; ++gi) mx[gi] = fmaxf(mx[gi], 1.f);
+    for (int gi = 0; gi < GV; ++gi) mx[gi] = __fdividef(1.f, fmaxf(mx[gi], 1.f));  // 1 / s
     float sq[NV], ss[GV];
 #pragma unroll
     for (int c = 0; c < NV; ++c) {
-      const float s = acc[c] / mx[c / GC];
+      const float s = acc[c] * mx[c / GC];
       sq[c] = s * s;
     }
     group_sum<NV, GV>(sq, ss, lpg);
 #pragma unroll
-    for (int gi = 0; gi < GV; ++gi)
-      ss[gi] = mx[gi] * sqrtf(ss[gi] * inv_g + eps / (mx[gi] * mx[gi]));
+    for (int gi = 0; gi < GV; ++gi) ss[gi] = mx[gi] * rsqrtf(ss[gi] * inv_g + eps * mx[gi] * mx[gi]);
 #pragma unroll
-    for (int c = 0; c < NV; ++c) acc[c] = acc[c] / ss[c / GC];
+    for (int c = 0; c < NV; ++c) acc[c] *= ss[c / GC];
   }
 }
 
