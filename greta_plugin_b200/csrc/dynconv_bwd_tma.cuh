@@ -11,10 +11,12 @@
 // Each persistent CTA (one per SM) owns a contiguous token range [u0, u1)
 // and a slice of dcta channels (all D when D <= bwd_rows_max_channels; else the
 // channels are split over nsplit CTAs that stream the same range). Its
-// producer warp streams the slice's token rows of x, the filters, dout (and
-// gate, saved pre-norm output) into a ring of shared-memory stages with
-// cp.async.bulk; completion is counted on each stage's "full"
-// mbarrier and consumers release a stage on its "empty" mbarrier. Each of the
+// producer (a warp of its own, or lane 0 of consumer warp 0) streams the
+// slice's token rows of x, the filters, dout (and gate, saved pre-norm output)
+// into a ring of shared-memory stages with cp.async.bulk; completion is
+// counted on each stage's "full" mbarrier and consumers release a stage on its
+// "empty" mbarrier. The inline producer refills the stage of tile i - 1 with
+// tile i - 1 + S once it has finished tile i, so it seldom waits. Each of the
 // dcta/8 consumer threads owns 8 channels for the whole range and walks it in
 // time order, keeping the last W-1 inputs (for dw and the conv recompute) and
 // W-1 partial dx rows in registers: dy[t] is scattered into the pending rows,
@@ -38,13 +40,25 @@
 namespace greta {
 
 // Widest filter of the row-streaming backward, and the most channels per CTA
-// for a filter-width template WT (exact W > 0, or -MAXW): W-1 pending dx rows
-// and W-1 inputs of a thread's 8 channels stay in registers, ~150 registers
-// per thread at W = 4 and more above, so a 1-CTA-per-SM launch has
-// 32 + 2048/8 threads (168 registers each) for W <= 4 and 32 + 1024/8
-// (255 registers) for wider filters.
+// for a filter-width template WT (exact W > 0, or -MAXW) and GV filter groups
+// per thread. W-1 pending dx rows and W-1 inputs of a thread's 8 channels stay
+// in registers: ~160 registers per thread at W = 4, ~210 at W = 7 with one
+// group per thread, up to 255 for the others. A scheduler (a quarter of the
+// SM's register file) holds two warps of 255 registers or three of 168, so:
+//   W <= 4          32 + 2048/8 threads (a producer warp + 8 consumer warps)
+//   W = 7, GV = 1   2048/8 threads, no producer warp: consumer warp 0 issues
+//                   the copies (bwd_rows_inline_producer)
+//   otherwise       32 + 1024/8 threads
+// A lone warp per scheduler leaves the long dependent chains of the wide
+// filters exposed; two hide much of them.
 constexpr int kMaxWBwdRows = 8;
-__host__ __device__ constexpr int bwd_rows_max_channels(int wt) { return (wt < 0 ? -wt : wt) <= 4 ? 2048 : 1024; }
+__host__ __device__ constexpr bool bwd_rows_inline_producer(int wt, int gv) { return wt == 7 && gv == 1; }
+__host__ __device__ constexpr int bwd_rows_max_channels(int wt, int gv) {
+  return ((wt < 0 ? -wt : wt) <= 4 || bwd_rows_inline_producer(wt, gv)) ? 2048 : 1024;
+}
+__host__ __device__ constexpr int bwd_rows_threads(int wt, int gv, int dcta) {
+  return (bwd_rows_inline_producer(wt, gv) ? 0 : 32) + dcta / kVec;
+}
 
 struct BwdRowsParams {
   const void* x;
@@ -72,8 +86,9 @@ struct BwdRowsParams {
 };
 
 template <typename T, int WT, int NORM, int GV>
-__global__ void __launch_bounds__(32 + bwd_rows_max_channels(WT) / kVec, 1)
+__global__ void __launch_bounds__(bwd_rows_threads(WT, GV, bwd_rows_max_channels(WT, GV)), 1)
     dynconv_bwd_rows_kernel(const BwdRowsParams p) {
+  constexpr bool INL = bwd_rows_inline_producer(WT, GV);
   constexpr int NV = kVec;
   constexpr int MAXW = WT > 0 ? WT : -WT;
   constexpr int MAXH = MAXW > 1 ? MAXW - 1 : 1;
@@ -88,7 +103,7 @@ __global__ void __launch_bounds__(32 + bwd_rows_max_channels(WT) / kVec, 1)
   const long long DC = D / G;
   const float inv_g = 1.f / (float)G;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nconsw = (int)(blockDim.x >> 5) - 1;  // consumer warps
+  const int nconsw = (int)(blockDim.x >> 5) - (INL ? 0 : 1);  // consumer warps
   const int S = p.stages;
 
   extern __shared__ __align__(128) unsigned char smem[];
@@ -137,11 +152,10 @@ __global__ void __launch_bounds__(32 + bwd_rows_max_channels(WT) / kVec, 1)
   const unsigned rowx = (unsigned)(dct * ES);
   const unsigned roww = p.wsplit ? (unsigned)(W * fct * ES) : (unsigned)(W * DC * ES);
 
-  if (warp == 0) {
-    // =========================== producer ===========================
-    if (lane != 0) return;
-    const unsigned per_row = 2u * rowx + roww + (gg != nullptr ? rowx : 0u) + (NORM != kNormNone ? rowx : 0u);
-    const unsigned sb0 = smem_addr(smem + p.off_stage);
+  // =========================== producer ===========================
+  const unsigned per_row = 2u * rowx + roww + (gg != nullptr ? rowx : 0u) + (NORM != kNormNone ? rowx : 0u);
+  // Issue tile i's copies into stage i % S (seen empty by the caller).
+  auto issue = [&](long long i) {
     const bool whole = p.nsplit == 1;  // slices are whole rows: one copy per tensor
     // n rows of a [T, D] tensor's slice, starting at token t
     auto copy_rows = [&](unsigned dst, const T* src, long long t, int n, unsigned bar) {
@@ -151,40 +165,44 @@ __global__ void __launch_bounds__(32 + bwd_rows_max_channels(WT) / kVec, 1)
         for (int j = 0; j < n; ++j) bulk_g2s(dst + j * rowx, src + (t + j) * D + c0, rowx, bar);
       }
     };
-    int s = 0;
-    unsigned par = 0;  // parity of the stage's current use
-    long long t0 = u0;
-    for (long long i = 0; i < ntiles; ++i, t0 += p.BT) {
-      if (i >= S && !mbar_wait(empty0 + 8 * s, par ^ 1u)) {
+    const int s = (int)(i % S);
+    const long long t0 = u0 + i * p.BT;
+    const int n = (int)min((long long)p.BT, ue - t0);
+    const unsigned bar = full0 + 8 * s;
+    const unsigned sb = smem_addr(smem + p.off_stage) + (unsigned)(s * p.stage_bytes);
+    mbar_arrive_expect_tx(bar, (unsigned)n * per_row);
+    copy_rows(sb, xg, t0, n, bar);
+    if (p.wsplit) {
+      const unsigned tapb = (unsigned)(fct * ES);
+      for (int j = 0; j < n; ++j)
+        for (int k = 0; k < W; ++k)
+          bulk_g2s(sb + p.so_w + j * roww + k * tapb, wg + ((t0 + j) * W + k) * DC + c0 / G, tapb, bar);
+    } else {
+      bulk_g2s(sb + p.so_w, wg + t0 * W * DC, (unsigned)n * roww, bar);
+    }
+    copy_rows(sb + p.so_do, dog, t0, n, bar);
+    if (gg != nullptr) copy_rows(sb + p.so_g, gg, t0, n, bar);
+    if (NORM != kNormNone) copy_rows(sb + p.so_yr, yrg, t0, n, bar);
+  };
+  // bounded wait until the consumers have released the stage use of tile i
+  auto released = [&](long long i) { return mbar_wait(empty0 + 8 * (int)(i % S), (unsigned)((i / S) & 1)); };
+
+  if (!INL && warp == 0) {
+    if (lane != 0) return;
+    for (long long i = 0; i < ntiles; ++i) {
+      if (i >= S && !released(i - S)) {
         atomicOr(&g_tma_errors, kErrTimeout);
         return;
       }
-      const int n = (int)min((long long)p.BT, ue - t0);
-      const unsigned bar = full0 + 8 * s;
-      const unsigned sb = sb0 + (unsigned)(s * p.stage_bytes);
-      if (++s == S) {
-        s = 0;
-        par ^= 1u;
-      }
-      mbar_arrive_expect_tx(bar, (unsigned)n * per_row);
-      copy_rows(sb, xg, t0, n, bar);
-      if (p.wsplit) {
-        const unsigned tapb = (unsigned)(fct * ES);
-        for (int j = 0; j < n; ++j)
-          for (int k = 0; k < W; ++k)
-            bulk_g2s(sb + p.so_w + j * roww + k * tapb, wg + ((t0 + j) * W + k) * DC + c0 / G, tapb, bar);
-      } else {
-        bulk_g2s(sb + p.so_w, wg + t0 * W * DC, (unsigned)n * roww, bar);
-      }
-      copy_rows(sb + p.so_do, dog, t0, n, bar);
-      if (gg != nullptr) copy_rows(sb + p.so_g, gg, t0, n, bar);
-      if (NORM != kNormNone) copy_rows(sb + p.so_yr, yrg, t0, n, bar);
+      issue(i);
     }
     return;
   }
+  if (INL && threadIdx.x == 0)
+    for (long long i = 0; i < min((long long)S, ntiles); ++i) issue(i);
 
   // =========================== consumers ===========================
-  const int cidx = (int)threadIdx.x - 32;
+  const int cidx = (int)threadIdx.x - (INL ? 0 : 32);
   const int d0 = c0 + cidx * NV;  // first channel of this thread
   const long long f0 = d0 / G;
   // this thread's operands in a stage: channel offset in the slice rows, and
@@ -406,6 +424,17 @@ __global__ void __launch_bounds__(32 + bwd_rows_max_channels(WT) / kVec, 1)
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(empty0 + 8 * cur_s);
+    if (INL && warp == 0 && it >= 1 && it - 1 + S < ntiles) {  // refill the stage of tile it - 1
+      int ok = 1;
+      if (lane == 0) {
+        ok = released(it - 1);
+        if (ok)
+          issue(it - 1 + S);
+        else
+          atomicOr(&g_tma_errors, kErrTimeout);
+      }
+      if (!__shfl_sync(0xffffffffu, ok, 0)) return;
+    }
   }
   if (ue > u0 && ue == rb) flush();  // the last request ended inside the range or its halo
 }

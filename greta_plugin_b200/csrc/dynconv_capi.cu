@@ -251,7 +251,7 @@ int try_rows_bwd(int dtype, BwdRowsParams p, int norm, void* stream) {
     if (!aligned(q, 16)) return -1;
   // the W template launch_bwd_rows picks: 4, 7 or -kMaxWBwdRows
   const int wt = W == 4 ? 4 : (W == 7 ? 7 : -kMaxWBwdRows);
-  const int64_t dcta = slice_channels(D, bwd_rows_max_channels(wt));
+  const int64_t dcta = slice_channels(D, bwd_rows_max_channels(wt, group_vec(kVec, G)));
   if (dcta == 0) return -1;
   const int64_t nsplit = D / dcta;
   if ((W * DC * es) % 16 != 0) return -1;
@@ -304,7 +304,7 @@ int try_rows_bwd(int dtype, BwdRowsParams p, int norm, void* stream) {
   if (ranges <= 0) return GRETA_OK;
   const size_t smem = off_stage + S * stage;
   return finish(run_bwd_rows(dtype, p, norm, group_vec(kVec, G), dim3((unsigned)(ranges * nsplit)),
-                             dim3((unsigned)(32 + dcta / kVec)), smem, stream));
+                             dim3((unsigned)bwd_rows_threads(wt, group_vec(kVec, G), (int)dcta)), smem, stream));
 }
 
 // A run must cover the W-1 history positions: a request's old slot taps are

@@ -219,7 +219,10 @@ def test_inference_channel_split(capi):
     (512, 4, 64, True, True, torch.bfloat16, [1, 2, 3, 300, 0, 64, 5]),
     (4096, 4, 1, False, False, torch.bfloat16, [700, 3, 1, 300]),      # 2 slices, filters per tap
     (4096, 4, 1, True, True, torch.bfloat16, [257, 2, 400]),
-    (2048, 7, 128, True, True, torch.bfloat16, [1, 6, 7, 8, 500, 0]),  # 2 slices of 1024, whole rows
+    (2048, 7, 128, True, True, torch.bfloat16, [1, 6, 7, 8, 5000, 0]),  # 1 slice, producer in warp 0
+    (4096, 7, 128, False, True, torch.bfloat16, [3000, 1, 999]),         # 2 slices, producer in warp 0
+    (4096, 7, 8, True, False, torch.bfloat16, [2000, 50]),               # the same, filters per tap
+    (2048, 7, 2, False, False, torch.bfloat16, [700, 5, 300]),           # 2 slices of 1024, producer warp
     (1024, 7, 16, False, True, torch.float16, [30, 31, 200]),
     (768, 3, 2, True, False, torch.float32, [5, 100, 1, 2]),           # 768 = 3 x 256: one slice
     (1024, 2, 4, False, True, torch.bfloat16, [1, 1, 1, 1, 90]),
