@@ -92,6 +92,7 @@ __global__ void __launch_bounds__(bwd_rows_threads(WT, GV, bwd_rows_max_channels
   constexpr int NV = kVec;
   constexpr int MAXW = WT > 0 ? WT : -WT;
   constexpr int MAXH = MAXW > 1 ? MAXW - 1 : 1;
+  constexpr int MAXP = MAXW <= 2 ? 2 : (MAXW <= 4 ? 4 : 8);  // MAXW rounded up to a power of two
   constexpr int GC = NV / GV;
   constexpr int ES = (int)sizeof(T);
   using PX = Pack<T, NV>;
@@ -211,7 +212,6 @@ __global__ void __launch_bounds__(bwd_rows_threads(WT, GV, bwd_rows_max_channels
   const int woff = (p.wsplit ? (d0 - c0) / G : d0 / G) * ES;
   const int wtap = p.wsplit ? fct : (int)DC;
   const int lpg = (GV == 1 && G > NV) ? G / NV : 1;
-  const bool dw_writer = GV > 1 || (cidx & (lpg - 1)) == 0;
   T* __restrict__ dxg = reinterpret_cast<T*>(p.dx);
   T* __restrict__ dwg = reinterpret_cast<T*>(p.dw);
   T* __restrict__ dgg = reinterpret_cast<T*>(p.dg);
@@ -347,25 +347,40 @@ __global__ void __launch_bounds__(bwd_rows_threads(WT, GV, bwd_rows_max_channels
 #pragma unroll
         for (int c = 0; c < NV; ++c) yc[c] = 0.f;
         T* dwrow = dwg + u * W * DC + f0;
+        // GV == 1: this thread's part of the group's dw for the input i steps
+        // back, summed over the group's lanes below (GV > 1: stored at once)
+        float part[MAXP];
 #pragma unroll
-        for (int i = MAXW - 1; i >= 0; --i) {
+        for (int i = MAXP - 1; i >= 0; --i) {
+          part[i] = 0.f;
           if (i < W) {
-            const PX& xs = (i == 0) ? xr : hw[i > 0 ? i - 1 : 0];
+            const PX& xs = (i == 0) ? xr : hw[i > 0 && i - 1 < MAXH ? i - 1 : 0];
             float prod[NV], sm[GV];
 #pragma unroll
             for (int c = 0; c < NV; c += 2)
               mul2(prod[c], prod[c + 1], dy[c], dy[c + 1], to_f(xs.v[c]), to_f(xs.v[c + 1]));
             if (NORM == kNormNone && gg != nullptr) {
 #pragma unroll
-              for (int c = 0; c < NV; ++c) yc[c] = fma_io(xs.v[c], wr[i].v[c / GC], yc[c]);
+              for (int c = 0; c < NV; ++c) yc[c] = fma_io(xs.v[c], wr[i < MAXW ? i : 0].v[c / GC], yc[c]);
             }
-            group_sum<NV, GV>(prod, sm, lpg);
-            if (dw_writer) {
+            group_local_sum<NV, GV>(prod, sm);
+            if (GV == 1) {
+              part[i] = sm[0];
+            } else {
               PW o;
 #pragma unroll
               for (int gi = 0; gi < GV; ++gi) o.v[gi] = from_f<T>(sm[gi]);
               st<T, GV>(dwrow + (long long)(W - 1 - i) * DC, o);
             }
+          }
+        }
+        if (GV == 1) {  // one group over lpg lanes: reduce-scatter the W sums
+          int base, cnt;
+          group_sum_scatter<MAXP>(part, lpg, lane, base, cnt);
+          if ((cidx & (lpg - 1)) < min(lpg, MAXP)) {
+#pragma unroll
+            for (int j = 0; j < MAXP; ++j)
+              if (j < cnt && base + j < W) dwrow[(long long)(W - 1 - base - j) * DC] = from_f<T>(part[j]);
           }
         }
         if (gg != nullptr) {

@@ -174,8 +174,9 @@ __device__ __forceinline__ float sigmoidf_(float v) { return __fdividef(1.f, 1.f
 // group reductions. NV channels per thread; GV groups per thread when G < NV
 // (GC = NV / GV channels each), else one group spread over lpg = G / NV lanes.
 // ---------------------------------------------------------------------------
+// The thread's part: out[gi] = sum of its GC channels of group gi, in order.
 template <int NV, int GV>
-__device__ __forceinline__ void group_sum(const float (&v)[NV], float (&out)[GV], int lpg) {
+__device__ __forceinline__ void group_local_sum(const float (&v)[NV], float (&out)[GV]) {
   constexpr int GC = NV / GV;
 #pragma unroll
   for (int gi = 0; gi < GV; ++gi) {
@@ -184,8 +185,56 @@ __device__ __forceinline__ void group_sum(const float (&v)[NV], float (&out)[GV]
     for (int c = 0; c < GC; ++c) s += v[gi * GC + c];
     out[gi] = s;
   }
-  if (GV == 1) {
-    for (int o = 1; o < lpg; o <<= 1) out[0] += __shfl_xor_sync(0xffffffffu, out[0], o);
+}
+
+// The butterfly over the lpg lanes of a group: lane bit 0 first, own + partner
+// at each step (lpg is warp-uniform; the steps are unrolled so that the
+// reductions of independent values can interleave).
+__device__ __forceinline__ void group_xlane_sum(float& v, int lpg) {
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1)
+    if (o < lpg) v += __shfl_xor_sync(0xffffffffu, v, o);
+}
+
+template <int NV, int GV>
+__device__ __forceinline__ void group_sum(const float (&v)[NV], float (&out)[GV], int lpg) {
+  group_local_sum<NV, GV>(v, out);
+  if (GV == 1) group_xlane_sum(out[0], lpg);
+}
+
+// P per-lane values summed over the lpg lanes of a group and left spread over
+// them (reduce-scatter): at the step over lane bit o, a lane keeps half of its
+// values (the upper half when its bit o is set), sends the partner the other
+// half and adds the partner's copy of the kept half; once one value is left the
+// steps continue as a butterfly. Afterwards lane r of the group (r < min(lpg, P)
+// holds distinct totals; the lanes above repeat them) holds the totals of
+// values base .. base + cnt - 1 in v[0 .. cnt). The pairing and the order of
+// each addition are group_xlane_sum's, so every total is bit-identical to it,
+// with P - 1 shuffles instead of P log2(lpg) when lpg >= P.
+template <int P>
+__device__ __forceinline__ void group_sum_scatter(float (&v)[P], int lpg, int lane, int& base, int& cnt) {
+  base = 0;
+  cnt = P;
+#pragma unroll
+  for (int s = 0; s < 5; ++s) {
+    const int o = 1 << s;
+    const int m = P >> s;  // values per lane before this step (compile-time once unrolled)
+    if (o < lpg) {
+      if (m >= 2) {
+        const int half = m >> 1;
+        const bool hi = (lane & o) != 0;
+#pragma unroll
+        for (int j = 0; j < half; ++j) {
+          const float send = hi ? v[j] : v[half + j];
+          const float keep = hi ? v[half + j] : v[j];
+          v[j] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+        }
+        if (hi) base += half;
+        cnt = half;
+      } else {
+        v[0] += __shfl_xor_sync(0xffffffffu, v[0], o);
+      }
+    }
   }
 }
 
@@ -200,7 +249,9 @@ __device__ __forceinline__ void group_max(const float (&v)[NV], float (&out)[GV]
     out[gi] = s;
   }
   if (GV == 1) {
-    for (int o = 1; o < lpg; o <<= 1) out[0] = fmaxf(out[0], __shfl_xor_sync(0xffffffffu, out[0], o));
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1)
+      if (o < lpg) out[0] = fmaxf(out[0], __shfl_xor_sync(0xffffffffu, out[0], o));
   }
 }
 
@@ -208,8 +259,9 @@ __device__ __forceinline__ void group_max(const float (&v)[NV], float (&out)[GV]
 //   plain : y * 1/sqrt(mean(y^2) + eps)               (greta/dynamic_conv.py:251-255)
 //   stable: s = max(max|y|, 1); y / (s * sqrt(mean((y/s)^2) + eps/s^2))
 //                                                    (greta_vllm/triton_conv.py:71-77)
-// The reciprocal square root and the division by s are the hardware's fast
-// forms (rsqrt, reciprocal), as in the reference kernels' tl.rsqrt.
+// The reciprocal square roots are the hardware's fast form, as the reference
+// kernels' tl.rsqrt; 1/s is rounded exactly, so that groups with s above 2^126
+// (where a fast reciprocal flushes to zero) stay finite.
 template <int NORM, int NV, int GV>
 __device__ __forceinline__ void apply_norm(float (&acc)[NV], int G, int lpg, float eps) {
   constexpr int GC = NV / GV;
@@ -229,7 +281,7 @@ __device__ __forceinline__ void apply_norm(float (&acc)[NV], int G, int lpg, flo
     for (int c = 0; c < NV; ++c) ab[c] = fabsf(acc[c]);
     group_max<NV, GV>(ab, mx, lpg);
 #pragma unroll
-    for (int gi = 0; gi < GV; ++gi) mx[gi] = __fdividef(1.f, fmaxf(mx[gi], 1.f));  // 1 / s
+    for (int gi = 0; gi < GV; ++gi) mx[gi] = __frcp_rn(fmaxf(mx[gi], 1.f));  // 1 / s, exact for s up to FLT_MAX
     float sq[NV], ss[GV];
 #pragma unroll
     for (int c = 0; c < NV; ++c) {

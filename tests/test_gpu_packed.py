@@ -71,6 +71,20 @@ def test_dtypes_and_norm(dtype, norm):
     run_and_check(b, norm=norm, dtype=dtype)
 
 
+@pytest.mark.parametrize("lengths", [[1, 3, 60], [1, 1, 1]])  # row-streaming and register kernels
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_stable_norm_huge_values(dtype, lengths):
+    """The overflow-safe norm of the vLLM path on inputs whose conv outputs are
+    ~3e37 (their squares overflow fp32, some group maxima exceed 2^126): finite
+    and within tolerance of the oracle."""
+    b = make_batch(lengths, [0, -1, 2], [1, 1, 1], 3, 256, 4, 4, dtype, seed=17)
+    for k in ("x", "logical"):
+        b[k] = (b[k].float() * 3e37).to(dtype)
+    b["state"].copy_(b["logical"].to(DEV))
+    out = run_and_check(b, norm=True, dtype=dtype)
+    assert torch.isfinite(out.float()).all()
+
+
 def test_prefill_config_varlen_1024():
     """Varlen chunked prefill: 8 sequences with lengths ~U[32, 256] (sum <= 1024),
     C=4096, K=4, state [64, 4096, 3] ~ N(0,1) read from 8 distinct slots."""

@@ -228,6 +228,8 @@ def test_inference_channel_split(capi):
     (1024, 2, 4, False, True, torch.bfloat16, [1, 1, 1, 1, 90]),
     (512, 8, 8, True, True, torch.bfloat16, [9, 8, 7, 150]),
     (256, 5, 128, True, True, torch.bfloat16, [4, 5, 6, 60]),
+    (512, 3, 128, True, True, torch.bfloat16, [3, 70, 1]),             # runtime W, 16 lanes per group
+    (512, 4, 32, False, True, torch.bfloat16, [2, 90]),                 # 4 lanes per group
     (512, 4, 1, True, False, torch.bfloat16, [1, 2, 3]),                # fewer tokens than SMs
 ])
 def test_training_backward(capi, D, W, G, norm, gate_on, dtype, lens):
