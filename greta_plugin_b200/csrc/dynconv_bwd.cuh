@@ -58,6 +58,8 @@ __global__ void __launch_bounds__(256) dynconv_bwd_kernel(const BwdParams p) {
   const long long DC = D / G;
   const float inv_g = 1.f / (float)G;
 
+  pdl_wait();
+  pdl_trigger();
   ChunkInfo ci;
   if (!resolve_bwd_chunk(p, ci)) return;
 

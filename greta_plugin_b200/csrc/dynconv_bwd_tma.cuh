@@ -119,6 +119,8 @@ __global__ void __launch_bounds__(bwd_rows_threads(WT, GV, bwd_rows_max_channels
     }
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
+  pdl_wait();
+  pdl_trigger();
   const bool packed = p.mode == kModePacked;
   if (packed)
     load_offsets(bnd, p.starts, p.starts_i64, p.nseq, p.T);

@@ -87,6 +87,17 @@ struct alignas(sizeof(T) * N) Pack {
   T v[N];
 };
 
+// Programmatic dependent launch. Every kernel here is launched with
+// programmatic stream serialization, so it may start while the kernel before
+// it in the stream is still running: pdl_wait() blocks until that kernel has
+// completed and its writes are visible, and must come before the first access
+// to global memory (an L2 prefetch, which returns no data, may precede it).
+// pdl_trigger() lets the next kernel in the stream launch once every CTA of
+// this grid has triggered or exited, so its launch overlaps this kernel's
+// work. Both are no-ops without a dependent or a primary.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
+
 __device__ __forceinline__ float to_f(float v) { return v; }
 __device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
 __device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }

@@ -233,6 +233,8 @@ __global__ void __launch_bounds__(256) dynconv_fwd_kernel(const FwdParams p) {
   const int G = p.G;
   const long long DC = D / G;
 
+  pdl_wait();
+  pdl_trigger();
   ChunkInfo ci;
   if (!resolve_fwd_chunk(p, ci, W)) return;
 

@@ -192,21 +192,6 @@ __global__ void __launch_bounds__(32 + fwd_rows_max_channels(WT) / kVec, 1)
   int* sslot = reinterpret_cast<int*>(smem + p.off_meta);  // per-request slot and initial flag (PACKED + state)
   signed char* sinit = reinterpret_cast<signed char*>(smem + p.off_meta + 4 * p.nseq);
 
-  // Speculative history: when the requests start at token 0, the range most
-  // likely starts at its nominal boundary u_spec inside a request, whose W-1
-  // previous input rows a consumer thread needs first. They are loaded here,
-  // before the sequence offsets arrive, and used if the guess was right.
-  const long long u_spec = (long long)range * p.nominal;
-  Pack<T, kVec> hspec[MAXH];
-#pragma unroll
-  for (int i = 0; i < MAXH; ++i) zero(hspec[i]);
-  if (threadIdx.x >= 32 && p.mode != kModeContext && u_spec >= H && u_spec <= p.U) {
-    const T* xs = reinterpret_cast<const T*>(p.x) + c0 + ((int)threadIdx.x - 32) * kVec;
-#pragma unroll
-    for (int i = 0; i < MAXH; ++i)
-      if (i < H) hspec[i] = ld<T, kVec>(xs + (u_spec - 1 - i) * D);
-  }
-
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(full0 + 8 * s, 1);
@@ -215,7 +200,9 @@ __global__ void __launch_bounds__(32 + fwd_rows_max_channels(WT) / kVec, 1)
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
   if (warp == 0 && lane >= 8 && lane < 12 && p.mode != kModeContext) {
-    // Start HBM on this CTA's rows before anything else: bulk L2 prefetch of
+    // Start HBM on this CTA's rows before anything else, even before the
+    // kernel ahead in the stream has finished (a prefetch returns no data,
+    // and L2 stays coherent with that kernel's writes): bulk L2 prefetch of
     // the first pf_rows rows of its nominal range (the range when the
     // requests cover all tokens; boundary moves shift it by < W-1 rows), and
     // a touch of its first output row. The staged copies then hit L2, so the
@@ -237,6 +224,24 @@ __global__ void __launch_bounds__(32 + fwd_rows_max_channels(WT) / kVec, 1)
       asm volatile("prefetch.global.L2 [%0];\n" ::"l"(reinterpret_cast<const T*>(p.y) + u * D + c0));
     }
   }
+  pdl_wait();
+  pdl_trigger();
+
+  // Speculative history: when the requests start at token 0, the range most
+  // likely starts at its nominal boundary u_spec inside a request, whose W-1
+  // previous input rows a consumer thread needs first. They are loaded here,
+  // before the sequence offsets arrive, and used if the guess was right.
+  const long long u_spec = (long long)range * p.nominal;
+  Pack<T, kVec> hspec[MAXH];
+#pragma unroll
+  for (int i = 0; i < MAXH; ++i) zero(hspec[i]);
+  if (threadIdx.x >= 32 && p.mode != kModeContext && u_spec >= H && u_spec <= p.U) {
+    const T* xs = reinterpret_cast<const T*>(p.x) + c0 + ((int)threadIdx.x - 32) * kVec;
+#pragma unroll
+    for (int i = 0; i < MAXH; ++i)
+      if (i < H) hspec[i] = ld<T, kVec>(xs + (u_spec - 1 - i) * D);
+  }
+
   if (p.mode == kModePacked) {
     // sequence offsets, and with a state the requests' slots and flags, all
     // loaded at once (the slots do not depend on the offsets)

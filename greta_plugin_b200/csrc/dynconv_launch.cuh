@@ -18,6 +18,25 @@ struct LaunchShape {
   size_t smem = 0;  // dynamic shared memory per CTA
 };
 
+// Launch with programmatic stream serialization: the kernel may start while
+// the kernel ahead of it in the stream finishes, and waits for it
+// (pdl_wait) before its first access to global memory. Captured into CUDA
+// graphs as a programmatic edge.
+template <typename P>
+cudaError_t launch_pdl(void (*k)(P), dim3 grid, dim3 block, size_t smem, cudaStream_t st, const P& p) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k, p);
+}
+
 // Raise a kernel's dynamic shared-memory limit when a launch needs more than
 // the default 48 KB (large W with wide CTAs, or fp32).
 template <typename K>
@@ -32,8 +51,7 @@ cudaError_t fwd_one(FwdParams p, const LaunchShape& s, cudaStream_t st) {
   cudaError_t e = allow_smem(k, s.smem);
   if (e != cudaSuccess) return e;
   p.nblk = s.nblk;
-  k<<<s.grid, s.block, s.smem, st>>>(p);
-  return cudaGetLastError();
+  return launch_pdl(k, s.grid, s.block, s.smem, st, p);
 }
 
 template <typename T, int NV, int WT, int NORM>
@@ -77,8 +95,7 @@ cudaError_t launch_fwd(const FwdParams& p, int nv, int norm, int gv, const Launc
 template <typename T, int NV, int WT, int NORM, int GV>
 cudaError_t bwd_one(BwdParams p, const LaunchShape& s, cudaStream_t st) {
   p.nblk = s.nblk;
-  dynconv_bwd_kernel<T, NV, WT, NORM, GV><<<s.grid, s.block, 0, st>>>(p);
-  return cudaGetLastError();
+  return launch_pdl(dynconv_bwd_kernel<T, NV, WT, NORM, GV>, s.grid, s.block, 0, st, p);
 }
 
 template <typename T, int NV, int WT, int NORM>
@@ -123,8 +140,7 @@ cudaError_t rows_one(const RowsParams& p, dim3 grid, dim3 block, size_t smem, cu
   auto k = dynconv_fwd_rows_kernel<T, WT, NORM, GV>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  k<<<grid, block, smem, st>>>(p);
-  return cudaGetLastError();
+  return launch_pdl(k, grid, block, smem, st, p);
 }
 
 template <typename T, int WT, int NORM>

@@ -14,8 +14,7 @@ cudaError_t bwd_rows_one(const BwdRowsParams& p, dim3 grid, dim3 block, size_t s
   auto k = dynconv_bwd_rows_kernel<T, WT, NORM, GV>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  k<<<grid, block, smem, st>>>(p);
-  return cudaGetLastError();
+  return launch_pdl(k, grid, block, smem, st, p);
 }
 
 template <typename T, int WT, int NORM>
