@@ -422,8 +422,13 @@ def run_greta(torch, vc, dev, args, dist, rank, world, peak):
 
 
 def run_e2e_prefill(torch, vc, dev, args, dist):
-    """Public API with host buffers: pinned H2D of the step's inputs, the call,
-    D2H of the output -- all inside the timed region."""
+    """Public API with host buffers: every step copies its inputs from pinned
+    host memory (H2D), makes the call and copies the output back (D2H), all
+    inside the timed region. Steps are pipelined the way a server would run
+    them: the inputs are double-buffered on the device, H2D runs on one copy
+    stream and D2H on another, so step i's D2H and kernel overlap step i+1's
+    H2D on the full-duplex link; the calls stay in order on the current
+    stream (they update the shared conv state in place)."""
     b = make_prefill(torch, dev, 4242, D=args.channels)
     hx = b["x"].cpu().pin_memory()
     hw = b["w"].cpu().pin_memory()
@@ -431,33 +436,56 @@ def run_e2e_prefill(torch, vc, dev, args, dist):
     hsl = b["slots"].cpu().pin_memory()
     hi = b["init"].cpu().pin_memory()
     hy = torch.empty(b["y"].shape, dtype=b["y"].dtype).pin_memory()
-    dx, dw = torch.empty_like(b["x"]), torch.empty_like(b["w"])
-    ds, dsl, di = torch.empty_like(b["starts"]), torch.empty_like(b["slots"]), torch.empty_like(b["init"])
+    host_in = (hx, hw, hs, hsl, hi)
+    bufs = [tuple(torch.empty_like(t, device=dev) for t in host_in) for _ in range(2)]
+    ys = [torch.empty_like(b["y"]) for _ in range(2)]
     state = b["state"]
+    comp = torch.cuda.current_stream()
+    up, down = torch.cuda.Stream(), torch.cuda.Stream()
+    loaded = [torch.cuda.Event() for _ in range(2)]
+    computed = [torch.cuda.Event() for _ in range(2)]
+    free = [torch.cuda.Event() for _ in range(2)]
+    for k in range(2):
+        free[k].record(comp)
 
-    def step():
-        dx.copy_(hx, non_blocking=True)
-        dw.copy_(hw, non_blocking=True)
-        ds.copy_(hs, non_blocking=True)
-        dsl.copy_(hsl, non_blocking=True)
-        di.copy_(hi, non_blocking=True)
-        y = vc.packed_dynamic_conv_triton(dx, dw, None, state, ds, dsl, di, b["G"], norm=False)
-        hy.copy_(y, non_blocking=True)
+    def step(i):
+        k = i % 2
+        up.wait_event(free[k])  # the kernel and D2H of step i-2 are done with buffer k
+        with torch.cuda.stream(up):
+            for d, h in zip(bufs[k], host_in):
+                d.copy_(h, non_blocking=True)
+        loaded[k].record(up)
+        comp.wait_event(loaded[k])
+        dx, dw, ds, dsl, di = bufs[k]
+        vc.packed_dynamic_conv_triton(dx, dw, None, state, ds, dsl, di, b["G"], norm=False, out=ys[k])
+        computed[k].record(comp)
+        down.wait_event(computed[k])
+        with torch.cuda.stream(down):
+            hy.copy_(ys[k], non_blocking=True)
+        free[k].record(down)
 
-    for _ in range(max(args.warmup, 3)):
-        step()
+    def drain():
+        comp.wait_stream(up)
+        comp.wait_stream(down)
+
+    for i in range(max(args.warmup, 3)):
+        step(i)
+    drain()
     torch.cuda.synchronize()
     barrier(dist)
     torch.cuda.synchronize()
     steps = args.e2e_steps
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s.record()
-    for _ in range(steps):
-        step()
-    e.record()
+    s.record(comp)
+    for k in range(2):  # the timed steps start from idle copy streams
+        free[k].record(comp)
+    for i in range(steps):
+        step(i)
+    drain()
+    e.record(comp)
     e.synchronize()
     sec = reduce_max(torch, dist, s.elapsed_time(e) / 1e3)
-    h2d = sum(t.numel() * t.element_size() for t in (hx, hw, hs, hsl, hi))
+    h2d = sum(t.numel() * t.element_size() for t in host_in)
     d2h = hy.numel() * hy.element_size()
     return dict(tokens_per_s=b["T"] * steps / sec, h2d=h2d, d2h=d2h, launches=steps)
 
