@@ -88,6 +88,16 @@ cudaError_t run_bwd(int dtype, const BwdParams& p, int nv, int norm, const Launc
   }
 }
 
+cudaError_t run_fwd_decode(int dtype, const FwdParams& p, int norm, const LaunchShape& s, void* stream) {
+  const int gv = group_vec(kVec, p.G);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case GRETA_DT_F32: return launch_fwd_decode_f32(p, norm, gv, s, st);
+    case GRETA_DT_F16: return launch_fwd_decode_f16(p, norm, gv, s, st);
+    default: return launch_fwd_decode_bf16(p, norm, gv, s, st);
+  }
+}
+
 long long cdiv(long long a, long long b) { return (a + b - 1) / b; }
 
 // Built-in CTA shapes per launch path: {threads along channels (tx), token
@@ -95,7 +105,8 @@ long long cdiv(long long a, long long b) { return (a + b - 1) / b; }
 // consecutive tokens and each thread walks one run. Long streams use 32x4
 // CTAs; the backward uses longer runs to amortise its W-1 row right halo;
 // packed prefill uses short runs so a ~1k-token batch spreads over the GPU;
-// decode has one token per request and uses wide CTAs.
+// decode has one token per request and uses 128-thread CTAs (the decode
+// kernel's limit) with chunks of 8 tokens for the occasional longer request.
 struct Shape {
   int tx, ty, L;
 };
@@ -106,7 +117,7 @@ constexpr Shape kDefaultShape[kPaths] = {
     {32, 4, 16},   // GRETA_PATH_INFERENCE
     {256, 1, 1},   // GRETA_PATH_DECODE_ROWS
     {32, 2, 8},    // GRETA_PATH_PACKED_PREFILL
-    {128, 1, 16},  // GRETA_PATH_PACKED_DECODE
+    {128, 1, 8},   // GRETA_PATH_PACKED_DECODE
 };
 Shape g_override[kPaths] = {};
 
@@ -513,6 +524,15 @@ int greta_dynconv_packed_state(int dtype, const void* x, const void* w, const vo
     tp.eps = eps;
     const int r = try_rows_fwd(dtype, tp, gate != nullptr, norm, stream);
     if (r >= 0) return r;
+  }
+  if (decode_like && nv == kVec && (W == 4 || W == 7) && sh.ty == 1 && sh.tx <= 128 && T < INT_MAX &&
+      num_slots < INT_MAX && (p.state == nullptr || p.st_layout == kStDS || p.st_layout == kStSD)) {
+    // decode kernel: each request's first chunk of C tokens (C >= W-1) on CTA
+    // row r < num_reqs, then at most (T-1)/C later chunks of longer requests
+    p.L = p.chunk = sh.L;
+    const long long chunks = num_reqs + (T - 1) / p.chunk;
+    if (chunks * (D / 8 + 1) > INT_MAX) return GRETA_ERR_INVALID_ARG;
+    return finish(run_fwd_decode(dtype, p, norm, make_shape(chunks, D, nv, sh.tx, 1), stream));
   }
   const long long chunks = cdiv(T, p.chunk) + num_reqs;
   if (chunks * (D / 8 + 1) > INT_MAX) return GRETA_ERR_INVALID_ARG;
