@@ -95,6 +95,19 @@ struct alignas(sizeof(T) * N) Pack {
 // pdl_trigger() lets the next kernel in the stream launch once every CTA of
 // this grid has triggered or exited, so its launch overlaps this kernel's
 // work. Both are no-ops without a dependent or a primary.
+// L2 prefetch of the line holding `p` (no data returned; L2 stays coherent
+// with the writes of a kernel still running ahead in the stream).
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];\n" ::"l"(p));
+}
+
+// Lines of [p, p + bytes) prefetched into L2 by `n` cooperating threads,
+// thread `i` taking every n-th 128-byte line.
+__device__ __forceinline__ void prefetch_l2_span(const void* p, long long bytes, int i, int n) {
+  const char* a = static_cast<const char*>(p);
+  for (long long o = (long long)i * 128; o < bytes; o += (long long)n * 128) prefetch_l2(a + o);
+}
+
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
 

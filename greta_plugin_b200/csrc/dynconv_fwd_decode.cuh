@@ -232,6 +232,26 @@ __device__ __forceinline__ void decode_run(const FwdParams& p, long long row) {
 template <typename T, int W, int NORM, int GV>
 __global__ void __launch_bounds__(128, decode_min_ctas<T>(W)) dynconv_fwd_decode_kernel(const FwdParams p) {
   const long long row = blockIdx.x / p.nblk;
+  if (row < p.nseq) {
+    // While the kernel ahead in the stream finishes: bring the request's
+    // metadata and the speculative first token's operands into L2, so that
+    // the loads after the wait are L2 hits.
+    const int d0 = ((int)(blockIdx.x % p.nblk) * blockDim.x + threadIdx.x) * kVec;
+    if (threadIdx.x == 0) {
+      prefetch_l2(reinterpret_cast<const char*>(p.starts) + (row << (p.starts_i64 ? 3 : 2)));
+      if (p.slots != nullptr) prefetch_l2(p.slots + row);
+      if (p.initial != nullptr) prefetch_l2(p.initial + row);
+    }
+    if (row < p.T && d0 < p.D) {
+      const T* xr = reinterpret_cast<const T*>(p.x) + row * p.D;
+      prefetch_l2(xr + d0);
+      if (p.g != nullptr) prefetch_l2(reinterpret_cast<const T*>(p.g) + row * p.D + d0);
+      const long long DC = p.D / p.G;
+      const T* wr = reinterpret_cast<const T*>(p.w) + row * W * DC + d0 / p.G;
+#pragma unroll
+      for (int k = 0; k < W; ++k) prefetch_l2(wr + k * DC);
+    }
+  }
   pdl_wait();
   pdl_trigger();
   if (p.st_layout == kStSD)

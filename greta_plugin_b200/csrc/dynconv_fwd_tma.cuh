@@ -221,7 +221,16 @@ __global__ void __launch_bounds__(32 + fwd_rows_max_channels(WT) / kVec, 1)
     } else if (lane == 9) {
       bulk_prefetch_l2(reinterpret_cast<const T*>(p.w) + u * W * DC, n * (unsigned)(W * DC * ES));
     } else if (lane == 11) {
-      asm volatile("prefetch.global.L2 [%0];\n" ::"l"(reinterpret_cast<const T*>(p.y) + u * D + c0));
+      prefetch_l2(reinterpret_cast<const T*>(p.y) + u * D + c0);
+    }
+  }
+  if (warp == 0 && lane >= 12 && p.mode == kModePacked) {
+    // the request metadata, read by every CTA right after the wait
+    const int i = lane - 12, n = 20;
+    prefetch_l2_span(p.starts, (p.nseq + 1) << (p.starts_i64 ? 3 : 2), i, n);
+    if (has_state) {
+      prefetch_l2_span(p.slots, p.nseq * 4, i, n);
+      prefetch_l2_span(p.initial, p.nseq, i, n);
     }
   }
   pdl_wait();
