@@ -225,12 +225,14 @@ int try_rows_fwd(int dtype, RowsParams p, bool gate, int norm, void* stream) {
   if (ranges < 1) ranges = 1;
   if (p.U < ranges) ranges = p.U;
   if (ranges <= 0) return GRETA_OK;
-  p.nominal = (p.U + ranges - 1) / ranges;
+  // balanced ranges: U / ranges tokens, the first U % ranges one longer
+  p.nominal = p.U / ranges;
+  p.nom_rem = (int)(p.U % ranges);
   // L2 prefetch at the start: the first rows of every range, about 48 MB in
   // all (a whole short prefill; the head of each range of a long stream)
   const int64_t full_row = D * es * (gate ? 2 : 1) + W * DC * es;
   int64_t pf = ((int64_t)48 << 20) / (ranges * full_row);
-  if (pf > p.nominal) pf = p.nominal;
+  if (pf > p.nominal + (p.nom_rem > 0)) pf = p.nominal + (p.nom_rem > 0);
   p.pf_rows = (int)(pf < 1 ? 1 : pf);
   const size_t smem = off_stage + S * stage;
   return finish(run_rows(dtype, p, norm, group_vec(kVec, G), dim3((unsigned)(ranges * nsplit)),

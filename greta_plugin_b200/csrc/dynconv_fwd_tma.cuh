@@ -48,7 +48,8 @@ struct RowsParams {
   long long U;     // tokens of the launch (T, or nseq * Q for CONTEXT)
   int D, W, G;
   int log2g;          // G = 1 << log2g
-  long long nominal;  // tokens per range before boundary moves: ceil(U / ranges)
+  long long nominal;  // tokens per range before boundary moves: U / ranges ...
+  int nom_rem;        // ... plus one for the first U % ranges ranges
   int pf_rows;        // rows of the range prefetched into L2 at the start (>= 1)
   int dcta;    // channels per CTA (a multiple of 256 dividing D)
   int nsplit;  // D / dcta: CTAs per token range
@@ -72,8 +73,17 @@ struct RowsParams {
 // ---------------------------------------------------------------------------
 // ranges
 // ---------------------------------------------------------------------------
-// Move a range boundary out of the first W-1 tokens of a request. The
-// requests cover tokens [ulo, uhi).
+// Nominal start of range r (before boundary moves), relative to the first
+// covered token: ranges of U / ranges tokens, the first U % ranges of them one
+// longer (no division on the device).
+__device__ __forceinline__ long long nominal_start(const RowsParams& p, int r) {
+  return (long long)r * p.nominal + min(r, p.nom_rem);
+}
+
+// Move a range boundary out of the first W-1 tokens of a request, to the
+// nearer of the request's start and its (W-1)-th token. The requests cover
+// tokens [ulo, uhi). The result is non-decreasing in v, so ranges stay
+// ordered and disjoint.
 __device__ __forceinline__ long long adjust_boundary(const RowsParams& p, const long long* bnd, long long v, int H,
                                                      long long uhi) {
   if (v >= uhi) return uhi;
@@ -87,7 +97,7 @@ __device__ __forceinline__ long long adjust_boundary(const RowsParams& p, const 
     b = bnd[s + 1];
   }
   const long long local = v - a;
-  if (local > 0 && local < H) v = min(a + H, b);
+  if (local > 0 && local < H) v = 2 * local <= H ? a : min(a + H, b);
   return v;
 }
 
@@ -207,7 +217,7 @@ __global__ void __launch_bounds__(32 + fwd_rows_max_channels(WT) / kVec, 1)
     // requests cover all tokens; boundary moves shift it by < W-1 rows), and
     // a touch of its first output row. The staged copies then hit L2, so the
     // stage ring refills at L2 latency while HBM streams continuously.
-    const long long u = min((long long)range * p.nominal, p.U - 1);
+    const long long u = min(nominal_start(p, range), p.U - 1);
     const unsigned n = (unsigned)min((long long)p.pf_rows, p.U - u);
     const T* xs = reinterpret_cast<const T*>(p.x) + u * D;
     const T* gs = p.g != nullptr ? reinterpret_cast<const T*>(p.g) + u * D : nullptr;
@@ -233,6 +243,47 @@ __global__ void __launch_bounds__(32 + fwd_rows_max_channels(WT) / kVec, 1)
       prefetch_l2_span(p.initial, p.nseq, i, n);
     }
   }
+  const T* __restrict__ xg = reinterpret_cast<const T*>(p.x);
+  const T* __restrict__ wg = reinterpret_cast<const T*>(p.w);
+  const T* __restrict__ gg = reinterpret_cast<const T*>(p.g);
+  const long long xrow_b = p.mode == kModeContext ? p.T + H : 0;  // context rows per batch row
+  // staged row sizes (bytes): a channel slice of x / gate, and the filters
+  // (the slice's per tap, or whole rows)
+  const int fct = p.dcta >> p.log2g;  // filters of the slice
+  const unsigned rowx = (unsigned)(p.dcta * ES);
+  const unsigned roww = p.wsplit ? (unsigned)(W * fct * ES) : (unsigned)(W * DC * ES);
+  const unsigned sb0 = smem_addr(smem + p.off_stage);
+  const bool whole = p.nsplit == 1;  // slices are whole rows
+
+  // Stage copies of tokens [t0, t0 + n) into the stage at shared address sb,
+  // completing on mbarrier bar: x rows (not in CONTEXT mode, whose rows the
+  // producer addresses per batch row), filters and gate rows.
+  auto issue_x = [&](long long t0, int n, unsigned sb, unsigned bar) {
+    if (whole) {
+      bulk_g2s(sb, xg + t0 * D, (unsigned)n * rowx, bar);
+    } else {
+      for (int j = 0; j < n; ++j) bulk_g2s(sb + j * rowx, xg + (t0 + j) * D + c0, rowx, bar);
+    }
+  };
+  auto issue_wg = [&](long long t0, int n, unsigned sb, unsigned bar) {
+    if (p.wsplit) {
+      const unsigned tapb = (unsigned)(fct * ES);
+      const long long fc0 = c0 >> p.log2g;
+      for (int j = 0; j < n; ++j)
+        for (int k = 0; k < W; ++k)
+          bulk_g2s(sb + p.so_w + j * roww + k * tapb, wg + ((t0 + j) * W + k) * DC + fc0, tapb, bar);
+    } else {
+      bulk_g2s(sb + p.so_w, wg + t0 * W * DC, (unsigned)n * roww, bar);
+    }
+    if (gg != nullptr) {
+      if (whole) {
+        bulk_g2s(sb + p.so_g, gg + t0 * D, (unsigned)n * rowx, bar);
+      } else {
+        for (int j = 0; j < n; ++j) bulk_g2s(sb + p.so_g + j * rowx, gg + (t0 + j) * D + c0, rowx, bar);
+      }
+    }
+  };
+
   pdl_wait();
   pdl_trigger();
 
@@ -240,7 +291,7 @@ __global__ void __launch_bounds__(32 + fwd_rows_max_channels(WT) / kVec, 1)
   // likely starts at its nominal boundary u_spec inside a request, whose W-1
   // previous input rows a consumer thread needs first. They are loaded here,
   // before the sequence offsets arrive, and used if the guess was right.
-  const long long u_spec = (long long)range * p.nominal;
+  const long long u_spec = nominal_start(p, range);
   Pack<T, kVec> hspec[MAXH];
 #pragma unroll
   for (int i = 0; i < MAXH; ++i) zero(hspec[i]);
@@ -270,22 +321,11 @@ __global__ void __launch_bounds__(32 + fwd_rows_max_channels(WT) / kVec, 1)
   }
 
   // this CTA's channel slice [c0, c0 + dcta) and token range inside the
-  // covered tokens [ulo, uhi): nominal ranges of p.nominal = ceil(U / ranges)
-  // tokens (set on the host: no division here)
+  // covered tokens [ulo, uhi)
   const long long ulo = p.mode == kModePacked ? bnd[0] : 0;
   const long long uhi = p.mode == kModePacked ? bnd[p.nseq] : p.U;
-  const long long u0 = adjust_boundary(p, bnd, ulo + (long long)range * p.nominal, H, uhi);
-  const long long u1 = adjust_boundary(p, bnd, ulo + (long long)(range + 1) * p.nominal, H, uhi);
-
-  const T* __restrict__ xg = reinterpret_cast<const T*>(p.x);
-  const T* __restrict__ wg = reinterpret_cast<const T*>(p.w);
-  const T* __restrict__ gg = reinterpret_cast<const T*>(p.g);
-  const long long xrow_b = p.mode == kModeContext ? p.T + H : 0;  // context rows per batch row
-  // staged row sizes (bytes): a channel slice of x / gate, and the filters
-  // (the slice's per tap, or whole rows)
-  const int fct = p.dcta >> p.log2g;  // filters of the slice
-  const unsigned rowx = (unsigned)(p.dcta * ES);
-  const unsigned roww = p.wsplit ? (unsigned)(W * fct * ES) : (unsigned)(W * DC * ES);
+  const long long u0 = adjust_boundary(p, bnd, ulo + nominal_start(p, range), H, uhi);
+  const long long u1 = adjust_boundary(p, bnd, ulo + nominal_start(p, range + 1), H, uhi);
   // CONTEXT: batch row and position of token u0 (token counts fit 32 bits)
   const int q0 = p.mode == kModeContext ? (int)((unsigned)u0 % (unsigned)p.T) : 0;
   const long long b0 = p.mode == kModeContext ? (long long)((unsigned)u0 / (unsigned)p.T) : 0;
@@ -293,8 +333,6 @@ __global__ void __launch_bounds__(32 + fwd_rows_max_channels(WT) / kVec, 1)
   if (warp == 0) {
     // =========================== producer ===========================
     if (lane != 0) return;
-    const unsigned sb0 = smem_addr(smem + p.off_stage);
-    const bool whole = p.nsplit == 1;  // slices are whole rows
     int s = 0;
     unsigned par = 0;  // parity of the stage's current use
     long long cb = b0;  // CONTEXT: batch row and position of the next token
@@ -321,27 +359,10 @@ __global__ void __launch_bounds__(32 + fwd_rows_max_channels(WT) / kVec, 1)
             ++cb;
           }
         }
-      } else if (whole) {
-        bulk_g2s(sb, xg + t0 * D, (unsigned)n * rowx, bar);
       } else {
-        for (int j = 0; j < n; ++j) bulk_g2s(sb + j * rowx, xg + (t0 + j) * D + c0, rowx, bar);
+        issue_x(t0, n, sb, bar);
       }
-      if (p.wsplit) {
-        const unsigned tapb = (unsigned)(fct * ES);
-        const long long fc0 = c0 >> p.log2g;
-        for (int j = 0; j < n; ++j)
-          for (int k = 0; k < W; ++k)
-            bulk_g2s(sb + p.so_w + j * roww + k * tapb, wg + ((t0 + j) * W + k) * DC + fc0, tapb, bar);
-      } else {
-        bulk_g2s(sb + p.so_w, wg + t0 * W * DC, (unsigned)n * roww, bar);
-      }
-      if (gg != nullptr) {
-        if (whole) {
-          bulk_g2s(sb + p.so_g, gg + t0 * D, (unsigned)n * rowx, bar);
-        } else {
-          for (int j = 0; j < n; ++j) bulk_g2s(sb + p.so_g + j * rowx, gg + (t0 + j) * D + c0, rowx, bar);
-        }
-      }
+      issue_wg(t0, n, sb, bar);
     }
     return;
   }

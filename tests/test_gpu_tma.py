@@ -131,6 +131,57 @@ def test_packed_prefill_with_state(capi, layout, W, G):
     assert np.array_equal(sa.float().cpu().numpy(), so)
 
 
+@pytest.mark.parametrize("D,W,G", [(256, 4, 1), (256, 7, 128), (4096, 7, 16)])
+@pytest.mark.parametrize("seed", range(6))
+def test_packed_prefill_range_boundaries(capi, D, W, G, seed):
+    """Prefill batches from ~100 to ~2400 tokens, so that the persistent CTAs
+    get 0 to ~16 tokens each and range boundaries fall everywhere inside the
+    requests: a boundary inside a request's first W-1 tokens moves to the
+    request's start or to its (W-1)-th token, and offsets that do not start at
+    token 0 shift every range off its nominal start (the speculative history
+    rows are then not used). TMA and register paths agree bit for bit on y
+    (the covered rows) and the state; with offsets from 0 both match the
+    oracle; no pipeline wait times out."""
+    from greta_plugin_b200 import packed_dynamic_conv_triton
+
+    g = torch.Generator().manual_seed(1000 + seed)
+    n_req = int(torch.randint(3, 20, (1,), generator=g))
+    lens = torch.randint(0, 260 if seed % 2 else 40, (n_req,), generator=g).tolist()
+    lens[0] = max(lens[0], 1)
+    lead = 0 if seed < 3 else int(torch.randint(1, 9, (1,), generator=g))  # rows before the first request
+    T = lead + sum(lens)
+    if T <= 2 * n_req:  # keep it prefill-like (the TMA path)
+        lens[0] += 2 * n_req
+        T = lead + sum(lens)
+    n_slots = n_req + 4
+    slots = torch.randperm(n_slots, generator=g)[:n_req].to(torch.int32)
+    slots[0] = -1
+    init = (torch.rand(n_req, generator=g) > 0.2).to(torch.int8)
+    x = rand(g, T, D).to(DEV)
+    w = rand(g, T, W, D // G, scale=0.5).to(DEV)
+    gate = rand(g, T, D).to(DEV)
+    logical = rand(g, n_slots, D, W - 1)
+    starts = torch.tensor([lead] + list(lead + np.cumsum(lens)), dtype=torch.int32, device=DEV)
+    sl, ini = slots.to(DEV), init.to(DEV)
+    outs = []
+    for tma in (True, False):
+        capi.set_tma(tma)
+        st = logical.to(DEV).clone()
+        y = torch.zeros(T, D, device=DEV, dtype=torch.bfloat16)
+        packed_dynamic_conv_triton(x, w, gate, st, starts, sl, ini, G, out=y)
+        torch.cuda.synchronize()
+        outs.append((y, st))
+    capi.set_tma(True)
+    (ya, sa), (yb, sb) = outs
+    assert torch.equal(ya[lead:], yb[lead:])
+    assert torch.equal(sa, sb)
+    if lead == 0:
+        yo, so = oracle.packed(to_np(x), to_np(w), to_np(gate), to_np(logical), starts.cpu().numpy(),
+                               slots.numpy(), init.numpy(), G, 2)
+        assert_close(ya, yo, torch.bfloat16)
+        assert np.array_equal(sa.float().cpu().numpy(), so)
+
+
 # --------------------------------------------------------------------------
 # channel-split launches (a token range streamed by several CTAs, one per
 # channel slice) and the row-streaming backward
