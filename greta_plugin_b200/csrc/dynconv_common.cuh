@@ -320,6 +320,110 @@ __device__ __forceinline__ void apply_norm(float (&acc)[NV], int G, int lpg, flo
   }
 }
 
+// apply_norm on two tokens' accumulators at once: the same arithmetic in the
+// same order for each (so each result is bit-identical to apply_norm's), with
+// the two tokens' group reductions interleaved so that their shuffle
+// latencies overlap.
+template <int NV, int GV>
+__device__ __forceinline__ void group_sum2(const float (&a)[NV], const float (&b)[NV], float (&oa)[GV],
+                                           float (&ob)[GV], int lpg) {
+  group_local_sum<NV, GV>(a, oa);
+  group_local_sum<NV, GV>(b, ob);
+  if (GV == 1) {
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1)
+      if (o < lpg) {
+        const float pa = __shfl_xor_sync(0xffffffffu, oa[0], o);
+        const float pb = __shfl_xor_sync(0xffffffffu, ob[0], o);
+        oa[0] += pa;
+        ob[0] += pb;
+      }
+  }
+}
+
+template <int NV, int GV>
+__device__ __forceinline__ void group_max2(const float (&a)[NV], const float (&b)[NV], float (&oa)[GV],
+                                           float (&ob)[GV], int lpg) {
+  constexpr int GC = NV / GV;
+#pragma unroll
+  for (int gi = 0; gi < GV; ++gi) {
+    float sa = a[gi * GC], sb = b[gi * GC];
+#pragma unroll
+    for (int c = 1; c < GC; ++c) {
+      sa = fmaxf(sa, a[gi * GC + c]);
+      sb = fmaxf(sb, b[gi * GC + c]);
+    }
+    oa[gi] = sa;
+    ob[gi] = sb;
+  }
+  if (GV == 1) {
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1)
+      if (o < lpg) {
+        const float pa = __shfl_xor_sync(0xffffffffu, oa[0], o);
+        const float pb = __shfl_xor_sync(0xffffffffu, ob[0], o);
+        oa[0] = fmaxf(oa[0], pa);
+        ob[0] = fmaxf(ob[0], pb);
+      }
+  }
+}
+
+template <int NORM, int NV, int GV>
+__device__ __forceinline__ void apply_norm2(float (&a)[NV], float (&b)[NV], int G, int lpg, float eps) {
+  constexpr int GC = NV / GV;
+  const float inv_g = 1.f / (float)G;  // G is a power of two: exact
+  if (NORM == kNormPlain) {
+    float qa[NV], qb[NV], sa[GV], sb[GV];
+#pragma unroll
+    for (int c = 0; c < NV; ++c) {
+      qa[c] = a[c] * a[c];
+      qb[c] = b[c] * b[c];
+    }
+    group_sum2<NV, GV>(qa, qb, sa, sb, lpg);
+#pragma unroll
+    for (int gi = 0; gi < GV; ++gi) {
+      sa[gi] = rsqrtf(sa[gi] * inv_g + eps);
+      sb[gi] = rsqrtf(sb[gi] * inv_g + eps);
+    }
+#pragma unroll
+    for (int c = 0; c < NV; ++c) {
+      a[c] *= sa[c / GC];
+      b[c] *= sb[c / GC];
+    }
+  } else if (NORM == kNormStable) {
+    float ba[NV], bb[NV], ma[GV], mb[GV];
+#pragma unroll
+    for (int c = 0; c < NV; ++c) {
+      ba[c] = fabsf(a[c]);
+      bb[c] = fabsf(b[c]);
+    }
+    group_max2<NV, GV>(ba, bb, ma, mb, lpg);
+#pragma unroll
+    for (int gi = 0; gi < GV; ++gi) {
+      ma[gi] = __frcp_rn(fmaxf(ma[gi], 1.f));
+      mb[gi] = __frcp_rn(fmaxf(mb[gi], 1.f));
+    }
+    float qa[NV], qb[NV], sa[GV], sb[GV];
+#pragma unroll
+    for (int c = 0; c < NV; ++c) {
+      const float ta = a[c] * ma[c / GC], tb = b[c] * mb[c / GC];
+      qa[c] = ta * ta;
+      qb[c] = tb * tb;
+    }
+    group_sum2<NV, GV>(qa, qb, sa, sb, lpg);
+#pragma unroll
+    for (int gi = 0; gi < GV; ++gi) {
+      sa[gi] = ma[gi] * rsqrtf(sa[gi] * inv_g + eps * ma[gi] * ma[gi]);
+      sb[gi] = mb[gi] * rsqrtf(sb[gi] * inv_g + eps * mb[gi] * mb[gi]);
+    }
+#pragma unroll
+    for (int c = 0; c < NV; ++c) {
+      a[c] *= sa[c / GC];
+      b[c] *= sb[c / GC];
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // chunk resolution
 // ---------------------------------------------------------------------------

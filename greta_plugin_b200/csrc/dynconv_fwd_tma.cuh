@@ -182,6 +182,9 @@ __global__ void __launch_bounds__(32 + fwd_rows_max_channels(WT) / kVec, 1)
   constexpr int ES = (int)sizeof(T);
   using PX = Pack<T, NV>;
   using PW = Pack<T, GV>;
+  // Two tokens per iteration where the CTA has registers to spare (narrow
+  // CTAs of wide filters, whose norm and gate work makes them latency bound).
+  constexpr bool kPairTokens = fwd_rows_max_channels(WT) <= 2048 && MAXW <= 8;
   const int W = WT > 0 ? WT : p.W;
   const int H = W - 1;
   const int D = p.D;
@@ -491,7 +494,7 @@ __global__ void __launch_bounds__(32 + fwd_rows_max_channels(WT) / kVec, 1)
     const unsigned char* xsp = stg + xoff;
     const unsigned char* wsp = stg + p.so_w + woff;
     const unsigned char* gsp = stg + p.so_g + xoff;
-    for (int j = 0; j < n; ++j, xsp += rowx, wsp += roww, gsp += rowx, yp += D) {
+    for (int j = 0; j < n;) {
       const long long u = t0 + j;
       if (p.mode == kModeContext) {
         if (u != u0 && cq == 0) {  // a new batch row: its history is its context
@@ -524,6 +527,79 @@ __global__ void __launch_bounds__(32 + fwd_rows_max_channels(WT) / kVec, 1)
 #pragma unroll
           for (int c = 0; c < NV; ++c) acc[c] = fma_io(xs.v[c], wc[k].v[c / GC], acc[c]);
         }
+      }
+      if (kPairTokens && p.mode != kModeContext && j + 1 < n && u + 1 < rb) {
+        // Token u+1 of the same request alongside token u, so that the two
+        // tokens' norm reductions and gates overlap. Its taps, oldest first
+        // as for a single token: the window shifted by one, then x[u], x[u+1].
+        const PX xn = *reinterpret_cast<const PX*>(xsp + rowx);
+#pragma unroll
+        for (int k = 0; k < MAXW; ++k) {
+          zero(wc[k]);
+          if (k < W) wc[k] = *reinterpret_cast<const PW*>(wsp + roww + koff[k]);
+        }
+        float acn[NV];
+#pragma unroll
+        for (int c = 0; c < NV; ++c) acn[c] = 0.f;
+#pragma unroll
+        for (int k = MAXW - 1; k >= 0; --k) {
+          if (k < W) {
+            const PX& xs = (k == 0) ? xn : (k == 1 ? xc : hw[k > 1 ? k - 2 : 0]);
+#pragma unroll
+            for (int c = 0; c < NV; ++c) acn[c] = fma_io(xs.v[c], wc[k].v[c / GC], acn[c]);
+          }
+        }
+        if (NORM != kNormNone) {
+          if (yrp != nullptr) {
+            PX o, q;
+#pragma unroll
+            for (int c = 0; c < NV; ++c) {
+              o.v[c] = from_f<T>(acc[c]);
+              q.v[c] = from_f<T>(acn[c]);
+            }
+            st<T, NV>(yrp, o);
+            st<T, NV>(yrp + D, q);
+            yrp += 2 * D;
+          }
+          apply_norm2<NORM, NV, GV>(acc, acn, G, lpg, p.eps);
+        }
+        if (gg != nullptr) {
+          const PX gv = *reinterpret_cast<const PX*>(gsp);
+          const PX gw = *reinterpret_cast<const PX*>(gsp + rowx);
+#pragma unroll
+          for (int c = 0; c < NV; ++c) {
+            const float gf = to_f(gv.v[c]), gn = to_f(gw.v[c]);
+            acc[c] = acc[c] * (gf * sigmoidf_(gf));
+            acn[c] = acn[c] * (gn * sigmoidf_(gn));
+          }
+        }
+        {
+          PX o, q;
+#pragma unroll
+          for (int c = 0; c < NV; ++c) {
+            o.v[c] = from_f<T>(acc[c]);
+            q.v[c] = from_f<T>(acn[c]);
+          }
+          st<T, NV>(yp, o);
+          st<T, NV>(yp + D, q);
+        }
+#pragma unroll
+        for (int k = MAXH - 1; k > 1; --k) hw[k] = hw[k - 2];
+        if (MAXH > 1) hw[1] = xc;
+        hw[0] = xn;
+        if (has_state && head_here && slot >= 0 && u + 1 == rb - 1) {
+          PX taps[MAXH];
+#pragma unroll
+          for (int h = 0; h < MAXH; ++h) taps[h] = sel(hw, H - 1 - h);
+          rows_store_taps<T, NV, WT, MAXH>(p, slot, d0, H, taps);
+          slot = -1;
+        }
+        j += 2;
+        xsp += 2 * rowx;
+        wsp += 2 * roww;
+        gsp += 2 * rowx;
+        yp += 2 * D;
+        continue;
       }
       if (NORM != kNormNone) {
         if (yrp != nullptr) {
@@ -561,6 +637,11 @@ __global__ void __launch_bounds__(32 + fwd_rows_max_channels(WT) / kVec, 1)
         rows_store_taps<T, NV, WT, MAXH>(p, slot, d0, H, taps);
         slot = -1;
       }
+      ++j;
+      xsp += rowx;
+      wsp += roww;
+      gsp += rowx;
+      yp += D;
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(empty0 + 8 * cur_s);
