@@ -383,7 +383,48 @@ def dynamic_causal_conv1d_decode(
     return y
 
 
+def triton_dynamic_causal_conv1d_autograd_from_context(
+    context: torch.Tensor,
+    weights: torch.Tensor,
+    gate: Optional[torch.Tensor],
+    group_size: int,
+    norm: bool,
+    eps: float,
+) -> torch.Tensor:
+    """HF autograd path from an explicit context, as ONE packed call.
+
+    Same signature, result and gradients as the reference's
+    triton_dynamic_causal_conv1d_autograd_from_context
+    (greta/modeling_greta.py:378-414), which runs the training kernel once per
+    batch row on that row's context ([Q + W - 1] rows, weights and gate
+    zero-padded over the W - 1 history rows) and keeps the last Q outputs.
+    Here the B context rows are packed into one stream of B sequences of
+    L = Q + W - 1 tokens (cu_seqlens = 0, L, 2L, ...): each sequence starts
+    with zero history, exactly like the per-row calls, so one forward and one
+    backward launch replace B of each.
+
+    context: [B, Q + W - 1, D]; weights: [B, Q, W, D // group_size];
+    gate: [B, Q, D] or None. Returns [B, Q, D].
+    """
+    B, Q, W, F = weights.shape
+    L = context.shape[1]
+    if context.ndim != 3 or context.shape[0] != B or L < Q:
+        raise ValueError(
+            f"context {tuple(context.shape)} must be [B, Q + W - 1, D] for weights {tuple(weights.shape)}")
+    H = L - Q  # history rows of each context row (W - 1)
+    D = context.shape[2]
+    # zero filters (and gates) on the history rows, as the per-row padding does
+    w_full = torch.nn.functional.pad(weights, (0, 0, 0, 0, H, 0)).reshape(B * L, W, F)
+    g_full = None
+    if gate is not None:
+        g_full = torch.nn.functional.pad(gate, (0, 0, H, 0)).reshape(1, B * L, D)
+    cu = torch.arange(0, B * L + 1, L, dtype=torch.int32, device=context.device)
+    out = dynamic_causal_conv1d(context.reshape(1, B * L, D), w_full, g_full, cu, group_size, norm, eps)
+    return out.view(B, L, D)[:, H:]
+
+
 __all__ = [
+    "triton_dynamic_causal_conv1d_autograd_from_context",
     "dynamic_causal_conv1d",
     "dynamic_causal_conv1d_decode",
     "dynamic_causal_conv1d_inference",

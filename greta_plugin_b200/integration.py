@@ -4,7 +4,9 @@ and state plumbing unchanged.
 Hugging Face: greta/modeling_greta.py binds the Triton entry points to
 module globals at import (modeling_greta.py:25-34) and GretaDynamicConv.forward
 (:437-569) calls them; install_hf() rebinds those globals (and the names in
-greta/dynamic_conv.py) to the functions of greta_plugin_b200.dynamic_conv.
+greta/dynamic_conv.py) to the functions of greta_plugin_b200.dynamic_conv, and
+replaces the per-batch-row autograd helper (modeling_greta.py:378-414) with a
+single packed call.
 
 vLLM: GretaConv.run_conv (greta_vllm/model.py:142-163) calls
 packed_dynamic_conv_triton when `triton_supports(G, D)` holds; install_vllm()
@@ -26,6 +28,9 @@ HF_GLOBALS = {
     "_TRITON_DYNAMIC_CAUSAL_CONV1D": _dc.dynamic_causal_conv1d,
     "_TRITON_DYNAMIC_CAUSAL_CONV1D_DECODE": _dc.dynamic_causal_conv1d_decode,
     "_TRITON_DYNAMIC_CAUSAL_CONV1D_INFERENCE": _dc.dynamic_causal_conv1d_inference,
+    # one packed call instead of the reference's loop over batch rows
+    # (greta/modeling_greta.py:378-414)
+    "triton_dynamic_causal_conv1d_autograd_from_context": _dc.triton_dynamic_causal_conv1d_autograd_from_context,
 }
 
 DYNAMIC_CONV_NAMES = {

@@ -78,3 +78,53 @@ def test_hf_decode_sequence_matches_prefill():
         yq = dynamic_causal_conv1d_decode(ctx[:, W - 1 + q].contiguous(), w[:, q].contiguous(), state,
                                           gate[:, q].contiguous(), G, True)
         torch.testing.assert_close(yq, y_full[:, q], rtol=0, atol=0)
+
+
+def _autograd_from_context_per_row(context, weights, gate, group_size, norm, eps):
+    """The reference's algorithm (greta/modeling_greta.py:378-414): one
+    training-kernel call per batch row on that row's context, filters and gate
+    zero-padded over the history rows, keeping the last Q outputs."""
+    from greta_plugin_b200 import dynamic_causal_conv1d
+
+    B, Q, W, F = weights.shape
+    L = context.shape[1]
+    outs = []
+    for b in range(B):
+        pw = weights.new_zeros((L, W, F))
+        pw[-Q:] = weights[b]
+        pg = None
+        if gate is not None:
+            pg = gate.new_zeros((1, L, gate.shape[-1]))
+            pg[:, -Q:] = gate[b:b + 1]
+        full = dynamic_causal_conv1d(context[b:b + 1].contiguous(), pw.contiguous(), pg, None, group_size, norm, eps)
+        outs.append(full[:, -Q:])
+    return torch.cat(outs, dim=0)
+
+
+@pytest.mark.parametrize("W,G,norm,gate_on", [(7, 128, True, True), (4, 1, False, False), (3, 8, True, False)])
+def test_autograd_from_context_one_packed_call(W, G, norm, gate_on):
+    """triton_dynamic_causal_conv1d_autograd_from_context as one packed call:
+    output and the gradients of context, weights and gate equal the per-row
+    loop of the reference's helper (within bf16 tolerance), and the output
+    matches the oracle's inference from context."""
+    from greta_plugin_b200.dynamic_conv import triton_dynamic_causal_conv1d_autograd_from_context as packed
+
+    g = torch.Generator().manual_seed(W * 13 + G)
+    B, Q, D = 3, 45, 256
+    ctx0 = rand(g, B, Q + W - 1, D)
+    w0 = rand(g, B, Q, W, D // G, scale=0.5)
+    g0 = rand(g, B, Q, D) if gate_on else None
+    dout = rand(g, B, Q, D).to(DEV)
+    results = []
+    for fn in (packed, _autograd_from_context_per_row):
+        ctx = ctx0.to(DEV).requires_grad_()
+        w = w0.to(DEV).requires_grad_()
+        gt = g0.to(DEV).requires_grad_() if gate_on else None
+        y = fn(ctx, w, gt, G, norm, 1e-6)
+        y.backward(dout)
+        results.append((y.detach(), ctx.grad, w.grad, None if gt is None else gt.grad))
+    for a, b in zip(results[0], results[1]):
+        if a is not None:
+            assert_close(a, b, torch.bfloat16)
+    yo = oracle.inference(to_np(ctx0), to_np(w0), to_np(g0), G, int(norm))
+    assert_close(results[0][0], yo, torch.bfloat16)

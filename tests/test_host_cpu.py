@@ -91,7 +91,8 @@ def _fake_reference(monkeypatch):
                                "dynamic_causal_conv1d_inference", "DynamicCausalConv1dFunction", "dynconv_fwd",
                                "dynconv_bwd"],
         "greta.modeling_greta": ["_TRITON_DYNAMIC_CAUSAL_CONV1D", "_TRITON_DYNAMIC_CAUSAL_CONV1D_DECODE",
-                                 "_TRITON_DYNAMIC_CAUSAL_CONV1D_INFERENCE"],
+                                 "_TRITON_DYNAMIC_CAUSAL_CONV1D_INFERENCE",
+                                 "triton_dynamic_causal_conv1d_autograd_from_context"],
         "greta_vllm": [],
         "greta_vllm.triton_conv": ["packed_dynamic_conv_triton", "supports"],
         "greta_vllm.model": ["packed_dynamic_conv_triton", "triton_supports"],
