@@ -115,7 +115,7 @@ constexpr Shape kDefaultShape[kPaths] = {
     {32, 4, 16},   // GRETA_PATH_FWD
     {32, 4, 32},   // GRETA_PATH_BWD
     {32, 4, 16},   // GRETA_PATH_INFERENCE
-    {256, 1, 1},   // GRETA_PATH_DECODE_ROWS
+    {128, 1, 1},   // GRETA_PATH_DECODE_ROWS
     {32, 2, 8},    // GRETA_PATH_PACKED_PREFILL
     {128, 1, 8},   // GRETA_PATH_PACKED_DECODE
 };
@@ -467,6 +467,8 @@ int greta_dynconv_decode_rows(int dtype, const void* x, const void* w, const voi
   p.st_layout = (nv == kVec && aligned(conv_state, (int64_t)kVec * es)) ? kStDS : kStGeneric;
   p.eps = eps;
   const Shape sh = shape_for(GRETA_PATH_DECODE_ROWS, H);
+  if (nv == kVec && (W == 4 || W == 7) && p.st_layout == kStDS && sh.tx <= 128)
+    return finish(run_fwd_decode(dtype, p, norm, make_shape(B, D, nv, sh.tx, 1), stream));
   return finish(run_fwd(dtype, p, nv, norm, make_shape(B, D, nv, sh.tx, 1), stream));
 }
 

@@ -27,6 +27,10 @@
 // the arithmetic (fp32 sums, taps oldest first) is the same, so both kernels
 // give identical bits. W is 4 or 7 (Greta's kernel size) and the state is DS
 // or SD; other shapes use dynconv_fwd_kernel.
+//
+// The same kernel serves the HF single-token decode (FwdParams::mode ROWS):
+// batch row r is one token whose history is state row r (DS), shifted in
+// place -- no request metadata at all.
 #pragma once
 
 #include "dynconv_fwd.cuh"
@@ -130,7 +134,20 @@ __device__ __forceinline__ void decode_run(const FwdParams& p, long long row) {
   bool has_old = false;
   TokenLoads<T, NV, GV, W> tok;  // operands of the token being convolved
   bool spec = false;             // tok already holds the request's first token
-  if (row < p.nseq) {
+  if (p.mode == kModeRows) {
+    // HF decode: batch row r is one token with history in state row r,
+    // shifted in place (greta/dynamic_conv.py:513-602); no metadata
+    if (row >= p.nseq) return;
+    const int r = (int)row;
+    load_token(tok, xg, wg, gg, r, r, D, W, DC, f0, d0, active);
+    a = r;
+    len = 1;
+    c1 = 1;
+    head = true;
+    spec = true;
+    slot = r;
+    has_old = true;
+  } else if (row < p.nseq) {
     const int r = (int)row;
     // speculative operands of token r, independent of the metadata
     if (r < p.T) load_token(tok, xg, wg, gg, r, r, D, W, DC, f0, d0, active);
@@ -232,7 +249,18 @@ __device__ __forceinline__ void decode_run(const FwdParams& p, long long row) {
 template <typename T, int W, int NORM, int GV>
 __global__ void __launch_bounds__(128, decode_min_ctas<T>(W)) dynconv_fwd_decode_kernel(const FwdParams p) {
   const long long row = blockIdx.x / p.nblk;
-  if (row < p.nseq) {
+  if (row < p.nseq && p.mode == kModeRows) {
+    // the row's operands, ahead of the wait (see below)
+    const int d0 = ((int)(blockIdx.x % p.nblk) * blockDim.x + threadIdx.x) * kVec;
+    if (d0 < p.D) {
+      prefetch_l2(reinterpret_cast<const T*>(p.x) + row * p.D + d0);
+      if (p.g != nullptr) prefetch_l2(reinterpret_cast<const T*>(p.g) + row * p.D + d0);
+      const long long DC = p.D / p.G;
+      const T* wr = reinterpret_cast<const T*>(p.w) + row * W * DC + d0 / p.G;
+#pragma unroll
+      for (int k = 0; k < W; ++k) prefetch_l2(wr + k * DC);
+    }
+  } else if (row < p.nseq) {
     // While the kernel ahead in the stream finishes: bring the request's
     // metadata and the speculative first token's operands into L2, so that
     // the loads after the wait are L2 hits.

@@ -102,3 +102,19 @@ def test_decode_config_greta_layer():
     b = make_batch([1] * 256, slots.tolist(), [1] * 256, 1024, 2048, 7, 128, torch.bfloat16, seed=5)
     run_and_check(b, norm=True)
     assert np.isfinite(b["state"].float().cpu().numpy()).all()
+
+
+def test_decode_out_of_range_slot_is_skipped_and_reported():
+    """A slot index >= the number of slots in a decode batch: the decode kernel
+    reads and writes no slot for that request (zero history) and raises the
+    error flag, which packed_dynamic_conv_checked reports as IndexError."""
+    from greta_plugin_b200.vllm_conv import packed_dynamic_conv_checked
+
+    b = make_batch([1, 1, 1, 1], [2, 99, 0, -1], [1, 1, 1, 1], 4, 256, 4, 1, torch.bfloat16, seed=31)
+    st = b["state"].clone()
+    with pytest.raises(IndexError):
+        packed_dynamic_conv_checked(b["x"].to(DEV), b["w"].to(DEV), b["gate"].to(DEV), b["state"],
+                                    b["starts"].to(DEV), b["slots"].to(DEV), b["init"].to(DEV), 1)
+    # slots 1 and 3 are named by no valid request: untouched
+    for s in (1, 3):
+        assert torch.equal(st[s], b["state"][s])

@@ -128,3 +128,29 @@ def test_autograd_from_context_one_packed_call(W, G, norm, gate_on):
             assert_close(a, b, torch.bfloat16)
     yo = oracle.inference(to_np(ctx0), to_np(w0), to_np(g0), G, int(norm))
     assert_close(results[0][0], yo, torch.bfloat16)
+
+
+@pytest.mark.parametrize("W,G,norm,gate_on", [(4, 1, False, False), (7, 128, True, True), (4, 8, True, True)])
+def test_decode_rows_kernels_bit_identical(W, G, norm, gate_on):
+    """HF decode rows run on the decode kernel (W = 4 or 7, contiguous state);
+    a 256-thread CTA shape, which that kernel does not take, forces the
+    register kernel: y and the shifted state agree bit for bit."""
+    from greta_plugin_b200 import _capi, dynamic_causal_conv1d_decode
+
+    g = torch.Generator().manual_seed(W + G)
+    B, D = 37, 1024
+    x = rand(g, B, D).to(DEV)
+    w = rand(g, B, W, D // G, scale=0.5).to(DEV)
+    gate = rand(g, B, D).to(DEV) if gate_on else None
+    state0 = rand(g, B, D, W - 1).to(DEV)
+    outs = []
+    try:
+        for shape in ((0, 0, 0), (256, 1, 1)):
+            _capi.set_launch_shape(3, *shape)  # GRETA_PATH_DECODE_ROWS
+            st = state0.clone()
+            y = dynamic_causal_conv1d_decode(x, w, st, gate, G, norm)
+            outs.append((y, st))
+    finally:
+        _capi.set_launch_shape(3)
+    assert torch.equal(outs[0][0].view(torch.int16), outs[1][0].view(torch.int16))
+    assert torch.equal(outs[0][1].view(torch.int16), outs[1][1].view(torch.int16))
