@@ -1,7 +1,7 @@
 """vLLM packed path (greta_vllm/triton_conv.py) on the GPU vs the CPU oracle:
 chunked prefill and decode with cache-slot history, padding slots (-1),
 has_initial off, chunks shorter than W-1, both vLLM state orientations and a
-generic strided state, the BASELINE-sized prefill and decode configurations,
+generic strided state, the benchmark-sized prefill and decode configurations,
 CUDA-graph capture, and out-of-range slot detection. Output within
 rtol = atol = 1e-2 (bf16); conv state bit-exact."""
 import numpy as np
