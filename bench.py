@@ -512,7 +512,8 @@ def cpu_prefill(seconds, threads):
             break
     del np
     return dict(value=b["T"] * n / el, unit="tokens/s", cores=threads, kind="port",
-                sample=f"{n} full prefill steps ({b['T']} tokens, C=4096, K=4, fp32 oracle) in {el:.1f} s")
+                sample=f"{n} full prefill steps ({b['T']} tokens, C=4096, K=4, fp32 oracle) in {el:.1f} s",
+                tokens=b["T"], lengths=b["lengths"])
 
 
 def cpu_decode(seconds, threads):
@@ -601,7 +602,9 @@ def config_block(args, world, prefill, greta=None):
             "seqs": 8, "tokens": prefill["tokens_per_step"] if prefill else None,
             "lengths": prefill.get("lengths") if prefill else None,
             "channels": args.channels, "kernel_size": 4, "group_size": 1, "norm": False, "gate": False,
-            "state_slots": 64, "l2": f"rotating {prefill['sets'] if prefill else '?'} input sets (> 2x L2)",
+            "state_slots": 64,
+            "l2": (f"rotating {prefill['sets']} input sets (> 2x L2)" if prefill and isinstance(prefill.get("sets"), int)
+                   else (prefill or {}).get("sets", "?")),
             "parallelism": par}
 
 
@@ -661,7 +664,9 @@ def main():
                 "warmup": args.warmup, "ms_per_step": 1e3 * 1 / res["value"] * 1, "higher_is_better": True,
                 "scaling": "weak" if args.shard == "requests" else "strong", "vs_baseline": None, "dtype": "f32",
                 "data": "synthetic (seeded N(0,1) inputs in the reference layouts)", "impl": "reference",
-                "config": config_block(args, 1, None),
+                "config": config_block(args, 1, {"tokens_per_step": res.pop("tokens"),
+                                                 "lengths": res.pop("lengths"),
+                                                 "sets": "one input set in host memory (CPU run, no GPU L2)"}),
                 "cpu_baseline": res,
                 "e2e": {"value": res["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         line["ms_per_step"] = None
@@ -701,6 +706,7 @@ def main():
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload in ("prefill", "all"):
         cpu = cpu_prefill(args.cpu_seconds, host_threads())
+        cpu.pop("tokens"), cpu.pop("lengths")
         if args.workload == "all":
             out.setdefault("decode", {})["cpu_baseline"] = cpu_decode(min(3.0, args.cpu_seconds), host_threads())
             out.setdefault("train", {})["cpu_baseline"] = cpu_train(min(10.0, args.cpu_seconds), host_threads())
