@@ -110,7 +110,7 @@ __device__ __forceinline__ void decode_token(const FwdParams& p, const TokenLoad
   }
 }
 
-template <bool DS, typename T, int W, int NORM, int GV>
+template <bool DS, bool ROWS, typename T, int W, int NORM, int GV>
 __device__ __forceinline__ void decode_run(const FwdParams& p, long long row) {
   constexpr int NV = kVec;
   constexpr int H = W - 1;
@@ -134,7 +134,7 @@ __device__ __forceinline__ void decode_run(const FwdParams& p, long long row) {
   bool has_old = false;
   TokenLoads<T, NV, GV, W> tok;  // operands of the token being convolved
   bool spec = false;             // tok already holds the request's first token
-  if (p.mode == kModeRows) {
+  if constexpr (ROWS) {
     // HF decode: batch row r is one token with history in state row r,
     // shifted in place (greta/dynamic_conv.py:513-602); no metadata
     if (row >= p.nseq) return;
@@ -246,10 +246,12 @@ __device__ __forceinline__ void decode_run(const FwdParams& p, long long row) {
   }
 }
 
-template <typename T, int W, int NORM, int GV>
+// ROWS: the HF decode (FwdParams::mode ROWS), a separate instantiation so
+// that the packed kernel's register allocation is its own.
+template <typename T, int W, int NORM, int GV, bool ROWS>
 __global__ void __launch_bounds__(128, decode_min_ctas<T>(W)) dynconv_fwd_decode_kernel(const FwdParams p) {
   const long long row = blockIdx.x / p.nblk;
-  if (row < p.nseq && p.mode == kModeRows) {
+  if (ROWS && row < p.nseq) {
     // the row's operands, ahead of the wait (see below)
     const int d0 = ((int)(blockIdx.x % p.nblk) * blockDim.x + threadIdx.x) * kVec;
     if (d0 < p.D) {
@@ -260,7 +262,7 @@ __global__ void __launch_bounds__(128, decode_min_ctas<T>(W)) dynconv_fwd_decode
 #pragma unroll
       for (int k = 0; k < W; ++k) prefetch_l2(wr + k * DC);
     }
-  } else if (row < p.nseq) {
+  } else if (!ROWS && row < p.nseq) {
     // While the kernel ahead in the stream finishes: bring the request's
     // metadata and the speculative first token's operands into L2, so that
     // the loads after the wait are L2 hits.
@@ -283,9 +285,9 @@ __global__ void __launch_bounds__(128, decode_min_ctas<T>(W)) dynconv_fwd_decode
   pdl_wait();
   pdl_trigger();
   if (p.st_layout == kStSD)
-    decode_run<false, T, W, NORM, GV>(p, row);
+    decode_run<false, ROWS, T, W, NORM, GV>(p, row);
   else
-    decode_run<true, T, W, NORM, GV>(p, row);
+    decode_run<true, ROWS, T, W, NORM, GV>(p, row);
 }
 
 }  // namespace greta

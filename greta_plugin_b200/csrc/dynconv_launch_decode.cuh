@@ -13,7 +13,8 @@ namespace greta {
 template <typename T, int WT, int NORM, int GV>
 cudaError_t decode_one(FwdParams p, const LaunchShape& s, cudaStream_t st) {
   p.nblk = s.nblk;
-  return launch_pdl(dynconv_fwd_decode_kernel<T, WT, NORM, GV>, s.grid, s.block, 0, st, p);
+  if (p.mode == kModeRows) return launch_pdl(dynconv_fwd_decode_kernel<T, WT, NORM, GV, true>, s.grid, s.block, 0, st, p);
+  return launch_pdl(dynconv_fwd_decode_kernel<T, WT, NORM, GV, false>, s.grid, s.block, 0, st, p);
 }
 
 template <typename T, int WT, int NORM>
