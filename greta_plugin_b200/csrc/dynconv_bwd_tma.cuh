@@ -324,18 +324,21 @@ __global__ void __launch_bounds__(bwd_rows_threads(WT, GV, bwd_rows_max_channels
         }
       }
       if (NORM == kNormPlain) {
-        float sq[NV], cs[GV];
+        // sum(yr^2) and sum(yr * dy) over the group in one interleaved
+        // reduction; sum(n * dy) = rinv * sum(yr * dy)
+        float sq[NV], py[NV], cs[GV];
 #pragma unroll
         for (int c = 0; c < NV; ++c) {
           const float yp = to_f(yrr.v[c]);
           sq[c] = yp * yp;
+          py[c] = yp * dy[c];
         }
-        group_sum<NV, GV>(sq, rinv, lpg);
+        group_sum2<NV, GV>(sq, py, rinv, cs, lpg);
 #pragma unroll
-        for (int gi = 0; gi < GV; ++gi) rinv[gi] = rsqrtf(rinv[gi] * inv_g + p.eps);
-#pragma unroll
-        for (int c = 0; c < NV; ++c) sq[c] = to_f(yrr.v[c]) * rinv[c / GC] * dy[c];
-        group_sum<NV, GV>(sq, cs, lpg);
+        for (int gi = 0; gi < GV; ++gi) {
+          rinv[gi] = rsqrtf(rinv[gi] * inv_g + p.eps);
+          cs[gi] *= rinv[gi];
+        }
 #pragma unroll
         for (int c = 0; c < NV; ++c) {
           const float nn = to_f(yrr.v[c]) * rinv[c / GC];
