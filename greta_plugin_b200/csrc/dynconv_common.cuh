@@ -279,6 +279,67 @@ __device__ __forceinline__ void group_max(const float (&v)[NV], float (&out)[GV]
   }
 }
 
+// Group max of a[] and group sum of b[] in one butterfly (each the same
+// arithmetic, in the same order, as group_max / group_sum).
+template <int NV, int GV>
+__device__ __forceinline__ void group_max_sum(const float (&a)[NV], const float (&b)[NV], float (&mx)[GV],
+                                              float (&sm)[GV], int lpg) {
+  constexpr int GC = NV / GV;
+  group_local_sum<NV, GV>(b, sm);
+#pragma unroll
+  for (int gi = 0; gi < GV; ++gi) {
+    float m = a[gi * GC];
+#pragma unroll
+    for (int c = 1; c < GC; ++c) m = fmaxf(m, a[gi * GC + c]);
+    mx[gi] = m;
+  }
+  if (GV == 1) {
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1)
+      if (o < lpg) {
+        const float pm = __shfl_xor_sync(0xffffffffu, mx[0], o);
+        const float ps = __shfl_xor_sync(0xffffffffu, sm[0], o);
+        mx[0] = fmaxf(mx[0], pm);
+        sm[0] += ps;
+      }
+  }
+}
+
+// The overflow-safe group RMS norm, given the group max of |y| (mx) and the
+// group sum of y^2 (ss). Its form s * sqrt(mean((y/s)^2) + eps/s^2), with
+// s = max(max|y|, 1), equals sqrt(mean(y^2) + eps): while every group of the
+// warp has max|y| <= 2^60 (squares, and their sums over at most 256 channels,
+// stay finite) that is what is computed; otherwise (or for a NaN) the warp
+// takes the rescaled two-pass form. For max|y| <= 1 both are the same
+// arithmetic. Must be called by all 32 lanes.
+template <int NV, int GV>
+__device__ __forceinline__ void stable_finish(float (&acc)[NV], float (&mx)[GV], float (&ss)[GV], int G, int lpg,
+                                              float eps) {
+  constexpr int GC = NV / GV;
+  const float inv_g = 1.f / (float)G;  // G is a power of two: exact
+  bool big = false;
+#pragma unroll
+  for (int gi = 0; gi < GV; ++gi) big = big || !(mx[gi] <= 0x1p60f);
+  if (__any_sync(0xffffffffu, big)) {
+#pragma unroll
+    for (int gi = 0; gi < GV; ++gi) mx[gi] = __frcp_rn(fmaxf(mx[gi], 1.f));  // 1 / s, exact for s up to FLT_MAX
+    float sq[NV];
+#pragma unroll
+    for (int c = 0; c < NV; ++c) {
+      const float s = acc[c] * mx[c / GC];
+      sq[c] = s * s;
+    }
+    group_sum<NV, GV>(sq, ss, lpg);
+#pragma unroll
+    for (int gi = 0; gi < GV; ++gi) ss[gi] = mx[gi] * rsqrtf(ss[gi] * inv_g + eps * mx[gi] * mx[gi]);
+  } else {
+#pragma unroll
+    for (int gi = 0; gi < GV; ++gi) ss[gi] = rsqrtf(ss[gi] * inv_g + eps);
+  }
+#pragma unroll
+  for (int c = 0; c < NV; ++c) acc[c] *= ss[c / GC];
+}
+
 // Group RMS norm of a thread's NV accumulators, in place.
 //   plain : y * 1/sqrt(mean(y^2) + eps)               (greta/dynamic_conv.py:251-255)
 //   stable: s = max(max|y|, 1); y / (s * sqrt(mean((y/s)^2) + eps/s^2))
@@ -300,23 +361,14 @@ __device__ __forceinline__ void apply_norm(float (&acc)[NV], int G, int lpg, flo
 #pragma unroll
     for (int c = 0; c < NV; ++c) acc[c] *= ss[c / GC];
   } else if (NORM == kNormStable) {
-    float ab[NV], mx[GV];
-#pragma unroll
-    for (int c = 0; c < NV; ++c) ab[c] = fabsf(acc[c]);
-    group_max<NV, GV>(ab, mx, lpg);
-#pragma unroll
-    for (int gi = 0; gi < GV; ++gi) mx[gi] = __frcp_rn(fmaxf(mx[gi], 1.f));  // 1 / s, exact for s up to FLT_MAX
-    float sq[NV], ss[GV];
+    float ab[NV], sq[NV], mx[GV], ss[GV];
 #pragma unroll
     for (int c = 0; c < NV; ++c) {
-      const float s = acc[c] * mx[c / GC];
-      sq[c] = s * s;
+      ab[c] = fabsf(acc[c]);
+      sq[c] = acc[c] * acc[c];
     }
-    group_sum<NV, GV>(sq, ss, lpg);
-#pragma unroll
-    for (int gi = 0; gi < GV; ++gi) ss[gi] = mx[gi] * rsqrtf(ss[gi] * inv_g + eps * mx[gi] * mx[gi]);
-#pragma unroll
-    for (int c = 0; c < NV; ++c) acc[c] *= ss[c / GC];
+    group_max_sum<NV, GV>(ab, sq, mx, ss, lpg);
+    stable_finish<NV, GV>(acc, mx, ss, G, lpg, eps);
   }
 }
 
@@ -341,29 +393,37 @@ __device__ __forceinline__ void group_sum2(const float (&a)[NV], const float (&b
   }
 }
 
+// group_max_sum for two tokens, their four reductions in one butterfly.
 template <int NV, int GV>
-__device__ __forceinline__ void group_max2(const float (&a)[NV], const float (&b)[NV], float (&oa)[GV],
-                                           float (&ob)[GV], int lpg) {
+__device__ __forceinline__ void group_max_sum2(const float (&a)[NV], const float (&b)[NV], const float (&c2)[NV],
+                                               const float (&d)[NV], float (&ma)[GV], float (&sb)[GV],
+                                               float (&mc)[GV], float (&sd)[GV], int lpg) {
   constexpr int GC = NV / GV;
+  group_local_sum<NV, GV>(b, sb);
+  group_local_sum<NV, GV>(d, sd);
 #pragma unroll
   for (int gi = 0; gi < GV; ++gi) {
-    float sa = a[gi * GC], sb = b[gi * GC];
+    float m = a[gi * GC], n = c2[gi * GC];
 #pragma unroll
     for (int c = 1; c < GC; ++c) {
-      sa = fmaxf(sa, a[gi * GC + c]);
-      sb = fmaxf(sb, b[gi * GC + c]);
+      m = fmaxf(m, a[gi * GC + c]);
+      n = fmaxf(n, c2[gi * GC + c]);
     }
-    oa[gi] = sa;
-    ob[gi] = sb;
+    ma[gi] = m;
+    mc[gi] = n;
   }
   if (GV == 1) {
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1)
       if (o < lpg) {
-        const float pa = __shfl_xor_sync(0xffffffffu, oa[0], o);
-        const float pb = __shfl_xor_sync(0xffffffffu, ob[0], o);
-        oa[0] = fmaxf(oa[0], pa);
-        ob[0] = fmaxf(ob[0], pb);
+        const float p0 = __shfl_xor_sync(0xffffffffu, ma[0], o);
+        const float p1 = __shfl_xor_sync(0xffffffffu, sb[0], o);
+        const float p2 = __shfl_xor_sync(0xffffffffu, mc[0], o);
+        const float p3 = __shfl_xor_sync(0xffffffffu, sd[0], o);
+        ma[0] = fmaxf(ma[0], p0);
+        sb[0] += p1;
+        mc[0] = fmaxf(mc[0], p2);
+        sd[0] += p3;
       }
   }
 }
@@ -391,36 +451,17 @@ __device__ __forceinline__ void apply_norm2(float (&a)[NV], float (&b)[NV], int 
       b[c] *= sb[c / GC];
     }
   } else if (NORM == kNormStable) {
-    float ba[NV], bb[NV], ma[GV], mb[GV];
+    float ba[NV], bb[NV], qa[NV], qb[NV], ma[GV], mb[GV], sa[GV], sb[GV];
 #pragma unroll
     for (int c = 0; c < NV; ++c) {
       ba[c] = fabsf(a[c]);
       bb[c] = fabsf(b[c]);
+      qa[c] = a[c] * a[c];
+      qb[c] = b[c] * b[c];
     }
-    group_max2<NV, GV>(ba, bb, ma, mb, lpg);
-#pragma unroll
-    for (int gi = 0; gi < GV; ++gi) {
-      ma[gi] = __frcp_rn(fmaxf(ma[gi], 1.f));
-      mb[gi] = __frcp_rn(fmaxf(mb[gi], 1.f));
-    }
-    float qa[NV], qb[NV], sa[GV], sb[GV];
-#pragma unroll
-    for (int c = 0; c < NV; ++c) {
-      const float ta = a[c] * ma[c / GC], tb = b[c] * mb[c / GC];
-      qa[c] = ta * ta;
-      qb[c] = tb * tb;
-    }
-    group_sum2<NV, GV>(qa, qb, sa, sb, lpg);
-#pragma unroll
-    for (int gi = 0; gi < GV; ++gi) {
-      sa[gi] = ma[gi] * rsqrtf(sa[gi] * inv_g + eps * ma[gi] * ma[gi]);
-      sb[gi] = mb[gi] * rsqrtf(sb[gi] * inv_g + eps * mb[gi] * mb[gi]);
-    }
-#pragma unroll
-    for (int c = 0; c < NV; ++c) {
-      a[c] *= sa[c / GC];
-      b[c] *= sb[c / GC];
-    }
+    group_max_sum2<NV, GV>(ba, qa, bb, qb, ma, sa, mb, sb, lpg);
+    stable_finish<NV, GV>(a, ma, sa, G, lpg, eps);
+    stable_finish<NV, GV>(b, mb, sb, G, lpg, eps);
   }
 }
 
