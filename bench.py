@@ -610,7 +610,9 @@ def config_block(args, world, prefill, greta=None):
 
 def profile_launches(args):
     """--ncu: each selected workload's kernels launched `steps` times after
-    `warmup` launches, on plain streams, so that ncu sees ordinary launches."""
+    `warmup` launches, on plain streams, so that ncu sees ordinary launches
+    (`greta`: the layer-shape training forward + backward, D=2048, W=7,
+    G=128, plain norm and gate)."""
     import torch
 
     from greta_plugin_b200 import _capi
@@ -642,6 +644,24 @@ def profile_launches(args):
                                                      args.train_seqs, T, D, W, G, 0, 1e-6, sp))
             _capi.check("bwd", lib.greta_dynconv_bwd(_capi.DT_BF16, P(x), P(w), None, None, P(dout), P(dx), P(dw),
                                                      None, P(cu), 0, args.train_seqs, T, D, W, G, 0, 1e-6, sp))
+    if args.workload == "greta":  # Greta's layer shape: training forward + backward, plain norm and gate
+        D, W, G, L = 2048, 7, 128, 4096
+        T = args.train_seqs * L
+        gd = torch.Generator(device=dev).manual_seed(3100)
+        x = torch.randn(T, D, device=dev, generator=gd).bfloat16()
+        g = torch.randn(T, D, device=dev, generator=gd).bfloat16()
+        w = (torch.randn(T, W, D // G, device=dev, generator=gd) * (1.0 / W) ** 0.5).bfloat16()
+        dout = torch.randn(T, D, device=dev, generator=gd).bfloat16()
+        y, yr, dx, dg, dw = (torch.empty_like(x), torch.empty_like(x), torch.empty_like(x), torch.empty_like(x),
+                             torch.empty_like(w))
+        cu = torch.arange(0, T + 1, L, dtype=torch.int32, device=dev)
+        lib, P, sp = _capi.lib(), _capi.ptr, _capi.stream_of(x)
+        for _ in range(n):
+            _capi.check("fwd", lib.greta_dynconv_fwd(_capi.DT_BF16, P(x), P(w), P(g), P(y), P(yr), P(cu), 0,
+                                                     args.train_seqs, T, D, W, G, _capi.NORM_PLAIN, 1e-6, sp))
+            _capi.check("bwd", lib.greta_dynconv_bwd(_capi.DT_BF16, P(x), P(w), P(g), P(yr), P(dout), P(dx), P(dw),
+                                                     P(dg), P(cu), 0, args.train_seqs, T, D, W, G, _capi.NORM_PLAIN,
+                                                     1e-6, sp))
     torch.cuda.synchronize()
 
 
