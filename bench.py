@@ -193,9 +193,19 @@ def packed_call(vc, b, out=None):
                                          b["G"], norm=False, eps=1e-6, out=b["y"] if out is None else out)
 
 
-def time_graph(torch, sets, launch, steps, warmup, dist):
+def hold_stream(torch, stream, us=200):
+    """Keep `stream` busy on the device for about `us` microseconds, so that
+    the host has submitted the work that follows before the start event after
+    this fires: the timed window then holds GPU time only, not the host's
+    submission latency (about 20 us for a graph replay)."""
+    with torch.cuda.stream(stream):
+        torch.cuda._sleep(int(us * 2.0e3))  # cycles at up to 2 GHz
+
+
+def time_graph(torch, sets, launch, steps, warmup, dist, spread=None):
     """Replay `steps` launches (rotating over `sets`) from one CUDA graph.
-    Returns seconds for the K timed steps (max over ranks)."""
+    Returns seconds for the K timed steps (max over ranks); `spread`, when
+    given, receives the min / median / max over ranks."""
     stream = torch.cuda.Stream()
     stream.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(stream):
@@ -213,6 +223,7 @@ def time_graph(torch, sets, launch, steps, warmup, dist):
     barrier(dist)
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    hold_stream(torch, stream)
     start.record(stream)
     with torch.cuda.stream(stream):
         graph.replay()
@@ -222,7 +233,20 @@ def time_graph(torch, sets, launch, steps, warmup, dist):
     barrier(dist)
     sec = start.elapsed_time(end) / 1e3
     del graph
+    if spread is not None:
+        spread.update(rank_spread(torch, dist, sec))
     return reduce_max(torch, dist, sec)
+
+
+def rank_spread(torch, dist, v):
+    """min / median / max of a per-rank value over the ranks."""
+    if dist is None:
+        return {"min": v, "median": v, "max": v, "ranks": 1}
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    out = [torch.zeros_like(t) for _ in range(dist.get_world_size())]
+    dist.all_gather(out, t)
+    vals = sorted(float(o.item()) for o in out)
+    return {"min": vals[0], "median": statistics.median(vals), "max": vals[-1], "ranks": len(vals)}
 
 
 def barrier(dist):
@@ -242,6 +266,33 @@ def n_sets(set_bytes):
     return max(2, math.ceil(2.5 * L2_BYTES / set_bytes))
 
 
+def time_isolated(torch, sets, launch, steps, dist):
+    """Per-call time of one launch with no programmatic-launch partner: each
+    step writes a 2.5 x L2 buffer (an L2 flush standing in for the GEMMs
+    around the conv in a model), then the call runs between two events. Plain
+    launches, no graph; the device is held while the host submits, so the
+    events time the kernel only. Returns the median step (max over ranks)."""
+    stream = torch.cuda.current_stream()
+    flush = torch.empty(int(2.5 * L2_BYTES) // 4, dtype=torch.float32, device="cuda")
+    n = max(5, min(steps, 50))
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
+    for i in range(3):
+        launch(sets[i % len(sets)])
+    torch.cuda.synchronize()
+    barrier(dist)
+    for i in range(n):
+        hold_stream(torch, stream, 100)
+        flush.zero_()
+        ev[i][0].record(stream)
+        launch(sets[i % len(sets)])
+        ev[i][1].record(stream)
+    torch.cuda.synchronize()
+    barrier(dist)
+    med = statistics.median(a.elapsed_time(b) / 1e3 for a, b in ev)
+    del flush
+    return reduce_max(torch, dist, med)
+
+
 # ---------------------------------------------------------------------------
 # workload runners
 # ---------------------------------------------------------------------------
@@ -253,12 +304,16 @@ def run_prefill(torch, vc, dev, args, dist, rank, world, peak, traffic):
     for i in range(n_sets(nbytes + probe["state"].numel() * 2)):
         sets.append(probe if i == 0 else make_prefill(torch, dev, base_seed + 97 * i, D=args.channels))
     steps = args.steps
-    sec = time_graph(torch, sets, lambda b: packed_call(vc, b), steps, args.warmup, dist)
+    spread = {}
+    sec = time_graph(torch, sets, lambda b: packed_call(vc, b), steps, args.warmup, dist, spread)
+    iso = time_isolated(torch, sets, lambda b: packed_call(vc, b), steps, dist)
     T = probe["T"]
     per_step = sec / steps
     achieved = nbytes / per_step / 1e9
     return dict(tokens_per_step=T, ms_per_step=per_step * 1e3, tokens_per_s=T / per_step, bytes_per_step=nbytes,
-                achieved_gbs=achieved, frac=achieved / peak, sets=len(sets), launches=steps,
+                achieved_gbs=achieved, frac=achieved / peak, sets=len(sets), launches=steps + max(5, min(steps, 50)),
+                us_per_step_over_ranks={k: (v / steps * 1e6 if k != "ranks" else v) for k, v in spread.items()},
+                isolated=dict(us=iso * 1e6, frac=nbytes / iso / 1e9 / peak),
                 lengths=probe["lengths"], traffic=traffic.get("prefill"))
 
 
@@ -269,11 +324,16 @@ def run_decode(torch, vc, dev, args, dist, rank, world, peak, traffic):
     set_bytes = nbytes + probe["state"].numel() * 2
     sets = [probe] + [make_decode(torch, dev, base_seed + 31 * i, D=args.channels) for i in range(1, n_sets(set_bytes))]
     steps = args.decode_steps
-    sec = time_graph(torch, sets, lambda b: packed_call(vc, b), steps, args.warmup, dist)
+    spread = {}
+    sec = time_graph(torch, sets, lambda b: packed_call(vc, b), steps, args.warmup, dist, spread)
+    iso = time_isolated(torch, sets, lambda b: packed_call(vc, b), steps, dist)
     per_step = sec / steps
     achieved = nbytes / per_step / 1e9
     return dict(tokens_per_step=probe["T"], ms_per_step=per_step * 1e3, tokens_per_s=probe["T"] / per_step,
-                bytes_per_step=nbytes, achieved_gbs=achieved, frac=achieved / peak, sets=len(sets), launches=steps,
+                bytes_per_step=nbytes, achieved_gbs=achieved, frac=achieved / peak, sets=len(sets),
+                launches=steps + max(5, min(steps, 50)),
+                us_per_step_over_ranks={k: (v / steps * 1e6 if k != "ranks" else v) for k, v in spread.items()},
+                isolated=dict(us=iso * 1e6, frac=nbytes / iso / 1e9 / peak),
                 traffic=traffic.get("decode"))
 
 
@@ -310,6 +370,7 @@ def run_train(torch, dev, args, dist, rank, world, peak, traffic):
     torch.cuda.synchronize()
     steps = args.train_steps
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(3 * steps)]
+    hold_stream(torch, stream)
     for i in range(steps):
         ev[3 * i].record(stream)
         fwd()
@@ -403,6 +464,7 @@ def run_greta(torch, vc, dev, args, dist, rank, world, peak):
     torch.cuda.synchronize()
     steps = args.train_steps
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(3 * steps)]
+    hold_stream(torch, stream)
     for i in range(steps):
         ev[3 * i].record(stream)
         fwd()
@@ -421,6 +483,106 @@ def run_greta(torch, vc, dev, args, dist, rank, world, peak):
     return out
 
 
+def run_reference_triton(torch, dev, args, dist, peak):
+    """The reference's own GPU kernels (Triton, from baseline/_ref, stock code
+    path) on the same B200, shapes and timing windows as the B200 kernels:
+    packed_dynamic_conv_triton (greta_vllm/triton_conv.py:128-173) on the
+    headline prefill and decode and at Greta's layer shape; dynconv_fwd /
+    dynconv_bwd (greta/dynamic_conv.py:786-864) on the training batch (their
+    autotuner runs during the warm-up). Informational: the reference arm of
+    the run is the CPU path."""
+    ref = import_reference()
+    if ref is None:
+        return {"unavailable": "baseline/_ref is not installed"}
+    if "triton_conv" not in ref:
+        return {"unavailable": ref.get("triton_error", "triton_conv did not import")}
+    rtc, rdc = ref["triton_conv"], ref["dynamic_conv"]
+    out = {"source": "baseline/_ref (unmodified Garbo-AI/greta-plugin), Triton kernels"}
+    D = args.channels
+
+    def packed(b, G=1, norm=False):
+        return rtc.packed_dynamic_conv_triton(b["x"], b["w"], b.get("gate"), b["state"], b["starts"], b["slots"],
+                                              b["init"], G, norm=norm, eps=1e-6, out=b["y"])
+
+    seed = 1000 + (int(os.environ.get("RANK", "0")) if args.shard == "requests" else 0)
+    probe = make_prefill(torch, dev, seed, D=D)
+    nb = prefill_bytes(probe)
+    sets = [probe] + [make_prefill(torch, dev, seed + 97 * i, D=D) for i in range(1, n_sets(nb + probe["state"].numel() * 2))]
+    sec = time_graph(torch, sets, packed, args.steps, args.warmup, dist) / args.steps
+    out["prefill"] = dict(tokens=probe["T"], us=sec * 1e6, tokens_per_s=probe["T"] / sec, frac=nb / sec / 1e9 / peak)
+    del sets, probe
+    probe = make_decode(torch, dev, 2000, D=D)
+    nb = decode_bytes(probe)
+    sets = [probe] + [make_decode(torch, dev, 2000 + 31 * i, D=D) for i in range(1, n_sets(nb + probe["state"].numel() * 2))]
+    sec = time_graph(torch, sets, packed, args.decode_steps, args.warmup, dist) / args.decode_steps
+    out["decode"] = dict(tokens=probe["T"], us=sec * 1e6, tokens_per_s=probe["T"] / sec, frac=nb / sec / 1e9 / peak)
+    del sets, probe
+
+    # Greta's layer shape on the packed path: D = 2048, W = 7, G = 128, norm + gate
+    Dg, Wg, Gg = 2048 // (args.world if args.shard == "channels" else 1), 7, 128
+
+    def with_gate(b, sd):
+        b["gate"] = torch.randn(b["T"], Dg, device=dev, generator=torch.Generator(device=dev).manual_seed(sd)).bfloat16()
+        return b
+
+    gl = {}
+    for name, mk, steps in (("prefill", make_prefill, args.steps), ("decode", make_decode, args.decode_steps)):
+        probe = with_gate(mk(torch, dev, 5000, D=Dg, W=Wg, G=Gg), 5000)
+        sets = [probe] + [with_gate(mk(torch, dev, 5000 + 31 * i, D=Dg, W=Wg, G=Gg), 5000 + 31 * i) for i in range(1, 6)]
+        sec = time_graph(torch, sets, lambda b: packed(b, Gg, True), steps, args.warmup, dist) / steps
+        gl[name] = dict(tokens=probe["T"], us=sec * 1e6, tokens_per_s=probe["T"] / sec)
+        del sets, probe
+
+    # training, both shapes: plain launches between events (the autotuner ran in the warm-up)
+    def train(Dt, Wt, Gt, norm, gate_on, seed_t):
+        S, L = args.train_seqs, 4096
+        T = S * L
+        gd = torch.Generator(device=dev).manual_seed(seed_t)
+        x = torch.randn(1, T, Dt, device=dev, generator=gd).bfloat16()
+        w = (torch.randn(T, Wt, Dt // Gt, device=dev, generator=gd) * (1.0 / Wt) ** 0.5).bfloat16()
+        g = torch.randn(1, T, Dt, device=dev, generator=gd).bfloat16() if gate_on else None
+        dout = torch.randn(1, T, Dt, device=dev, generator=gd).bfloat16()
+        cu_cpu = torch.arange(0, T + 1, L, dtype=torch.int32)
+        cu = cu_cpu.to(dev)
+        state = {}
+
+        def fwd():
+            y, yr, BT, ci = rdc.dynconv_fwd(x, w, g, cu, Gt, norm=norm, eps=1e-6, save_pre=norm, cu_seqlens_cpu=cu_cpu)
+            state.update(yr=yr, BT=BT, ci=ci)
+
+        def bwd():
+            rdc.dynconv_bwd(x, w, g, state["yr"], dout, cu, Gt, norm, 1e-6, state["BT"], state["ci"])
+
+        stream = torch.cuda.current_stream()
+        for _ in range(max(args.warmup, 3)):
+            fwd()
+            bwd()
+        torch.cuda.synchronize()
+        barrier(dist)
+        steps = args.train_steps
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3 * steps)]
+        for i in range(steps):
+            hold_stream(torch, stream, 100)
+            ev[3 * i].record(stream)
+            fwd()
+            ev[3 * i + 1].record(stream)
+            bwd()
+            ev[3 * i + 2].record(stream)
+        torch.cuda.synchronize()
+        barrier(dist)
+        f = reduce_max(torch, dist, statistics.median(ev[3 * i].elapsed_time(ev[3 * i + 1]) for i in range(steps)))
+        bk = reduce_max(torch, dist, statistics.median(ev[3 * i + 1].elapsed_time(ev[3 * i + 2]) for i in range(steps)))
+        return dict(tokens=T, fwd_us=f * 1e3, bwd_us=bk * 1e3)
+
+    tr = train(D, 4, 1, False, False, 3000)
+    tr["fwd_frac"] = tr["tokens"] * 12 * D / (tr["fwd_us"] * 1e-6) / 1e9 / peak
+    tr["bwd_frac"] = tr["tokens"] * 22 * D / (tr["bwd_us"] * 1e-6) / 1e9 / peak
+    out["train"] = tr
+    gl["train"] = train(Dg, Wg, Gg, True, True, 3100)
+    out["greta_layer"] = gl
+    return out
+
+
 def run_e2e_prefill(torch, vc, dev, args, dist):
     """Public API with host buffers: every step copies its inputs from pinned
     host memory (H2D), makes the call and copies the output back (D2H), all
@@ -429,7 +591,8 @@ def run_e2e_prefill(torch, vc, dev, args, dist):
     stream and D2H on another, so step i's D2H and kernel overlap step i+1's
     H2D on the full-duplex link; the calls stay in order on the current
     stream (they update the shared conv state in place)."""
-    b = make_prefill(torch, dev, 4242, D=args.channels)
+    b = make_prefill(torch, dev, 1000 + (int(os.environ.get("RANK", "0")) if args.shard == "requests" else 0),
+                     D=args.channels)  # the headline batch (898 tokens on rank 0)
     hx = b["x"].cpu().pin_memory()
     hw = b["w"].cpu().pin_memory()
     hs = b["starts"].cpu().pin_memory()
@@ -487,7 +650,20 @@ def run_e2e_prefill(torch, vc, dev, args, dist):
     sec = reduce_max(torch, dist, s.elapsed_time(e) / 1e3)
     h2d = sum(t.numel() * t.element_size() for t in host_in)
     d2h = hy.numel() * hy.element_size()
-    return dict(tokens_per_s=b["T"] * steps / sec, h2d=h2d, d2h=d2h, launches=steps)
+    # the link's own rate for this step's copies: the same H2D copies alone,
+    # back to back (pinned host memory -> device)
+    torch.cuda.synchronize()
+    barrier(dist)
+    s.record(up)
+    with torch.cuda.stream(up):
+        for _ in range(steps):
+            for d, h in zip(bufs[0], host_in):
+                d.copy_(h, non_blocking=True)
+    e.record(up)
+    e.synchronize()
+    h2d_sec = reduce_max(torch, dist, s.elapsed_time(e) / 1e3)
+    return dict(tokens_per_s=b["T"] * steps / sec, h2d=h2d, d2h=d2h, launches=steps, tokens=b["T"],
+                h2d_gbs=h2d * steps / sec / 1e9, h2d_copy_only_gbs=h2d * steps / h2d_sec / 1e9)
 
 
 # ---------------------------------------------------------------------------
@@ -558,6 +734,69 @@ def cpu_train(seconds, threads):
                 sample=f"{n} fwd+bwd passes over one 4096-token sequence (of 8) in {el:.1f} s")
 
 
+REF_DIR = ROOT / "baseline" / "_ref"
+
+
+def import_reference():
+    """Import the unmodified reference installed in baseline/_ref (the driver's
+    offline install of Garbo-AI/greta-plugin); None when it is not there."""
+    if not (REF_DIR / "greta_vllm" / "conv.py").is_file():
+        return None
+    if str(REF_DIR) not in sys.path:
+        sys.path.insert(0, str(REF_DIR))
+    import greta.dynamic_conv as rdc
+    import greta_vllm.conv as rconv
+
+    out = {"conv": rconv, "dynamic_conv": rdc}
+    try:
+        import greta_vllm.triton_conv as rtc
+
+        out["triton_conv"] = rtc
+    except Exception as exc:  # Triton missing: the CPU path still runs
+        out["triton_error"] = f"{type(exc).__name__}: {exc}"
+    return out
+
+
+def cpu_model():
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return None
+
+
+def cpu_prefill_reference(seconds, threads):
+    """The reference's own CPU path on the headline prefill: its pure-torch
+    packed_dynamic_conv (greta_vllm/conv.py:10-70) from baseline/_ref, fp32
+    inputs, all host threads, a fresh state clone per step (the call updates
+    the state in place). None when the reference is not installed."""
+    import torch
+
+    ref = import_reference()
+    if ref is None:
+        return None
+    torch.set_num_threads(threads)
+    b = make_prefill(torch, "cpu", 1000)
+    x, w, st0 = (b[k].float() for k in ("x", "w", "state"))
+    starts, slots, init = b["starts"], b["slots"], b["init"]
+    fn = ref["conv"].packed_dynamic_conv
+    fn(x[:64], w[:64], None, st0.clone(), torch.tensor([0, 64], dtype=torch.int32), slots[:1], init[:1], 1,
+       norm=False)  # warm
+    n, t0 = 0, time.perf_counter()
+    while True:
+        fn(x, w, None, st0.clone(), starts, slots, init, 1, norm=False)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds or n >= 10000:
+            break
+    return dict(value=b["T"] * n / el, unit="tokens/s", cores=threads, kind="reference", cpu_model=cpu_model(),
+                sample=f"{n} full prefill steps ({b['T']} tokens, C=4096, K=4) of greta_vllm.conv.packed_dynamic_conv"
+                       f" (fp32, torch {torch.__version__}, {threads} threads) in {el:.1f} s",
+                tokens=b["T"], lengths=b["lengths"])
+
+
 def host_threads():
     try:
         return len(os.sched_getaffinity(0))
@@ -579,6 +818,8 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-reference-triton", action="store_true",
+                    help="skip timing the reference's Triton kernels on the GPU (informational leg)")
     ap.add_argument("--ncu", action="store_true",
                     help="profiling mode: plain launches (no CUDA graph), no e2e or CPU arm, no JSON line")
     ap.add_argument("--train-seqs", type=int, default=8,
@@ -674,22 +915,26 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     args.channels = 4096 // world if (args.shard == "channels" and world > 1) else 4096
+    args.world = world
 
     if args.impl == "reference":
         if rank != 0:
             return
         threads = host_threads()
-        res = cpu_prefill(min(args.cpu_seconds, 30.0), threads)
+        # the reference's own CPU code (baseline/_ref), else its restatement
+        res = cpu_prefill_reference(min(args.cpu_seconds, 30.0), threads) or cpu_prefill(min(args.cpu_seconds, 30.0),
+                                                                                          threads)
         line = {"metric": METRIC, "value": res["value"], "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
-                "warmup": args.warmup, "ms_per_step": 1e3 * 1 / res["value"] * 1, "higher_is_better": True,
+                "warmup": args.warmup, "ms_per_step": 1e3 * res["tokens"] / res["value"], "higher_is_better": True,
                 "scaling": "weak" if args.shard == "requests" else "strong", "vs_baseline": None, "dtype": "f32",
                 "data": "synthetic (seeded N(0,1) inputs in the reference layouts)", "impl": "reference",
+                "source": ("greta_vllm.conv.packed_dynamic_conv from baseline/_ref (the reference's own torch CPU path)"
+                           if res["kind"] == "reference" else "oracle/ (the reference algorithm restated in C)"),
                 "config": config_block(args, 1, {"tokens_per_step": res.pop("tokens"),
                                                  "lengths": res.pop("lengths"),
                                                  "sets": "one input set in host memory (CPU run, no GPU L2)"}),
                 "cpu_baseline": res,
                 "e2e": {"value": res["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-        line["ms_per_step"] = None
         print(json.dumps(line))
         return
 
@@ -722,11 +967,23 @@ def main():
             out["greta_layer"] = run_greta(torch, vc, dev, args, dist, rank, world, peak)
         e2e = run_e2e_prefill(torch, vc, dev, args, dist) if args.workload in ("prefill", "all") else None
     clk = clocks.summary()
+    if args.workload == "all" and not args.no_reference_triton and world == 1:
+        try:
+            out["reference_triton"] = run_reference_triton(torch, dev, args, dist, peak)
+        except Exception as exc:  # informational leg: report, do not fail the run
+            out["reference_triton"] = {"error": f"{type(exc).__name__}: {exc}"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload in ("prefill", "all"):
-        cpu = cpu_prefill(args.cpu_seconds, host_threads())
-        cpu.pop("tokens"), cpu.pop("lengths")
+        port = cpu_prefill(args.cpu_seconds, host_threads())
+        port.pop("tokens"), port.pop("lengths")
+        port["cpu_model"] = cpu_model()
+        cpu = cpu_prefill_reference(args.cpu_seconds, host_threads())
+        if cpu is None:
+            cpu = port
+        else:
+            cpu.pop("tokens"), cpu.pop("lengths")
+            cpu["port"] = port
         if args.workload == "all":
             out.setdefault("decode", {})["cpu_baseline"] = cpu_decode(min(3.0, args.cpu_seconds), host_threads())
             out.setdefault("train", {})["cpu_baseline"] = cpu_train(min(10.0, args.cpu_seconds), host_threads())
@@ -768,7 +1025,10 @@ def main():
                          "frac_of_8tbs_spec": head["achieved_gbs"] / 8000.0},
             "cpu_baseline": cpu,
             "e2e": None if e2e is None else {"value": e2e["tokens_per_s"] * scale, "unit": "tokens/s",
-                                             "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"]},
+                                             "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"],
+                                             "tokens_per_step": e2e["tokens"], "h2d_gbs_per_gpu": e2e["h2d_gbs"],
+                                             "h2d_copy_only_gbs_per_gpu": e2e["h2d_copy_only_gbs"],
+                                             "bound": "host-to-device copies (PCIe)"},
             "gpu_launches": launches,
             "clocks": clk,
             "workloads": out,

@@ -5,8 +5,10 @@ fallback: if the library is missing or a call fails, an exception is raised.
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes
 import os
+import threading
 from pathlib import Path
 
 import torch
@@ -20,6 +22,38 @@ OK, ERR_INVALID_ARG, ERR_UNSUPPORTED, ERR_ALIGNMENT, ERR_LAUNCH = 0, 1, 2, 3, 4
 _DTYPES = {torch.float32: DT_F32, torch.float16: DT_F16, torch.bfloat16: DT_BF16}
 
 _lib = None
+
+
+class Options(ctypes.Structure):
+    """greta_dynconv_options: per-call launch choices of the `_ex` entry points."""
+    _fields_ = [("size", ctypes.c_int), ("register_path", ctypes.c_int), ("block_x", ctypes.c_int),
+                ("block_y", ctypes.c_int), ("tokens", ctypes.c_int), ("wait_limit_log2", ctypes.c_int),
+                ("test_withhold_release", ctypes.c_int)]
+
+
+_local = threading.local()
+
+
+@contextlib.contextmanager
+def launch_options(register_path=False, block_x=0, block_y=0, tokens=0, wait_limit_log2=0,
+                   test_withhold_release=False):
+    """Launch choices for the C-ABI calls this thread makes inside the block
+    (tests and tuning sweeps). They travel with each call as its options
+    argument; nothing is set in the library."""
+    o = Options(ctypes.sizeof(Options), int(bool(register_path)), block_x, block_y, tokens, wait_limit_log2,
+                int(bool(test_withhold_release)))
+    prev = getattr(_local, "opts", None)
+    _local.opts = o
+    try:
+        yield o
+    finally:
+        _local.opts = prev
+
+
+def options():
+    """The options of the enclosing launch_options block (None = defaults)."""
+    o = getattr(_local, "opts", None)
+    return None if o is None else ctypes.byref(o)
 
 
 class GretaKernelError(RuntimeError):
@@ -41,21 +75,24 @@ def lib() -> ctypes.CDLL:
             "(there is no CPU or Triton fallback)")
     L = ctypes.CDLL(str(LIB_PATH))
     P, I64, I32, F = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_float
-    L.greta_dynconv_fwd.argtypes = [I32, P, P, P, P, P, P, I32, I64, I64, I64, I64, I64, I32, F, P]
-    L.greta_dynconv_bwd.argtypes = [I32, P, P, P, P, P, P, P, P, P, I32, I64, I64, I64, I64, I64, I32, F, P]
-    L.greta_dynconv_inference.argtypes = [I32, P, P, P, P, I64, I64, I64, I64, I64, I32, F, P]
-    L.greta_dynconv_decode_rows.argtypes = [I32, P, P, P, P, P, I64, I64, I64, I64, I32, F, P]
-    L.greta_dynconv_packed_state.argtypes = [I32, P, P, P, P, P, I64, I64, I64, I64, P, P, P, I64, I64, I64, I64,
-                                             I64, I32, F, P, P]
+    sig = {
+        "fwd": [I32, P, P, P, P, P, P, I32, I64, I64, I64, I64, I64, I32, F, P],
+        "bwd": [I32, P, P, P, P, P, P, P, P, P, I32, I64, I64, I64, I64, I64, I32, F, P],
+        "inference": [I32, P, P, P, P, I64, I64, I64, I64, I64, I32, F, P],
+        "decode_rows": [I32, P, P, P, P, P, I64, I64, I64, I64, I32, F, P],
+        "packed_state": [I32, P, P, P, P, P, I64, I64, I64, I64, P, P, P, I64, I64, I64, I64, I64, I32, F, P, P],
+    }
+    for name, args in sig.items():
+        getattr(L, f"greta_dynconv_{name}").argtypes = args
+        getattr(L, f"greta_dynconv_{name}_ex").argtypes = args + [P]
+        getattr(L, f"greta_dynconv_{name}").restype = I32
+        getattr(L, f"greta_dynconv_{name}_ex").restype = I32
     L.greta_dynconv_supports.argtypes = [I64, I64]
-    L.greta_dynconv_set_launch_shape.argtypes = [I32, I32, I32, I32]
-    L.greta_dynconv_set_tma.argtypes = [I32]
     L.greta_dynconv_device_errors.argtypes = [I32]
     L.greta_dynconv_status_string.argtypes = [I32]
     L.greta_dynconv_status_string.restype = ctypes.c_char_p
     L.greta_dynconv_version.restype = I32
-    for name in ("fwd", "bwd", "inference", "decode_rows", "packed_state", "supports", "set_launch_shape", "set_tma",
-                 "device_errors"):
+    for name in ("supports", "device_errors"):
         getattr(L, f"greta_dynconv_{name}").restype = I32
     _lib = L
     return L
@@ -84,17 +121,18 @@ def check(fn: str, status: int) -> None:
         raise GretaKernelError(fn, status, msg)
 
 
-PATH_FWD, PATH_BWD, PATH_INFERENCE, PATH_DECODE_ROWS, PATH_PACKED_PREFILL, PATH_PACKED_DECODE = range(6)
+ERR_BIT_TIMEOUT = 2  # a pipeline wait of a row-streaming kernel ran out
 
 
-def set_launch_shape(path: int, block_x: int = 0, block_y: int = 0, tokens: int = 0) -> None:
-    """Override (or, with zeros, restore) the CTA shape of one launch path."""
-    check("greta_dynconv_set_launch_shape", lib().greta_dynconv_set_launch_shape(path, block_x, block_y, tokens))
-
-
-def set_tma(enable: bool) -> None:
-    """Use (default) or bypass the TMA-staged forward for long token streams."""
-    lib().greta_dynconv_set_tma(1 if enable else 0)
+def check_device_errors(fn: str) -> None:
+    """Raise GretaKernelError when an earlier kernel on the current device
+    recorded an error (clears the bits; synchronises the device)."""
+    bits = device_errors(clear=True)
+    if bits < 0:
+        raise GretaKernelError(fn, ERR_LAUNCH, "the device error word could not be read")
+    if bits & ERR_BIT_TIMEOUT:
+        raise GretaKernelError(fn, ERR_LAUNCH, "a pipeline wait timed out; the kernel returned with its outputs "
+                               "partly unwritten")
 
 
 def device_errors(clear: bool = True) -> int:

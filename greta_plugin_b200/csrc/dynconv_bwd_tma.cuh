@@ -81,6 +81,7 @@ struct BwdRowsParams {
   int BT;      // token rows per stage
   int stages;  // ring depth (<= kMaxStages)
   float eps;
+  int wait_log2;  // pipeline wait bound: 2^wait_log2 polls (0 = default)
   // shared-memory layout (bytes from the dynamic base)
   int off_bnd, off_stage, stage_bytes, so_w, so_do, so_g, so_yr;
 };
@@ -188,7 +189,10 @@ __global__ void __launch_bounds__(bwd_rows_threads(WT, GV, bwd_rows_max_channels
     if (NORM != kNormNone) copy_rows(sb + p.so_yr, yrg, t0, n, bar);
   };
   // bounded wait until the consumers have released the stage use of tile i
-  auto released = [&](long long i) { return mbar_wait(empty0 + 8 * (int)(i % S), (unsigned)((i / S) & 1)); };
+  const unsigned wlimit = wait_limit(p.wait_log2);
+  auto released = [&](long long i) {
+    return mbar_wait(empty0 + 8 * (int)(i % S), (unsigned)((i / S) & 1), wlimit);
+  };
 
   if (!INL && warp == 0) {
     if (lane != 0) return;
@@ -267,7 +271,7 @@ __global__ void __launch_bounds__(bwd_rows_threads(WT, GV, bwd_rows_max_channels
   unsigned par = 0;
   long long t0 = u0;
   for (long long it = 0; it < ntiles; ++it, t0 += p.BT) {
-    if (!mbar_wait(full0 + 8 * s, par)) {
+    if (!mbar_wait(full0 + 8 * s, par, wlimit)) {
       if (lane == 0) atomicOr(&g_tma_errors, kErrTimeout);
       return;
     }

@@ -6,6 +6,7 @@
 #include <climits>
 #include <initializer_list>
 
+#include "dynconv_fwd_wide.cuh"
 #include "dynconv_launch.cuh"
 #include "greta_dynconv.h"
 
@@ -13,7 +14,7 @@ using namespace greta;
 
 namespace {
 
-constexpr int kAbiVersion = 10000;  // 1.0.0
+constexpr int kAbiVersion = 10100;  // 1.1.0: per-call options (_ex), wide groups on the packed call
 
 int esize(int dtype) {
   switch (dtype) {
@@ -28,12 +29,14 @@ bool is_pow2(int64_t v) { return v > 0 && (v & (v - 1)) == 0; }
 
 bool aligned(const void* p, int64_t a) { return p == nullptr || (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
-int check_common(int dtype, int64_t D, int64_t W, int64_t G, int norm) {
+// max_g: the widest group the entry point takes (256, or D for the packed
+// call, whose wide groups run on dynconv_fwd_wide_kernel)
+int check_common(int dtype, int64_t D, int64_t W, int64_t G, int norm, int64_t max_g = 256) {
   if (esize(dtype) == 0) return GRETA_ERR_UNSUPPORTED;
   if (D <= 0 || W <= 0 || G <= 0) return GRETA_ERR_INVALID_ARG;
   if (D > (int64_t)INT_MAX / 2) return GRETA_ERR_INVALID_ARG;
   if (D % G != 0) return GRETA_ERR_INVALID_ARG;
-  if (!is_pow2(G) || G > 256) return GRETA_ERR_UNSUPPORTED;
+  if (!is_pow2(G) || G > max_g) return GRETA_ERR_UNSUPPORTED;
   if (W > kMaxWGeneric) return GRETA_ERR_UNSUPPORTED;
   if (norm < GRETA_NORM_NONE || norm > GRETA_NORM_STABLE) return GRETA_ERR_UNSUPPORTED;
   return GRETA_OK;
@@ -98,6 +101,15 @@ cudaError_t run_fwd_decode(int dtype, const FwdParams& p, int norm, const Launch
   }
 }
 
+cudaError_t run_fwd_wide(int dtype, const FwdParams& p, int norm, dim3 grid, dim3 block, int groups, void* stream) {
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case GRETA_DT_F32: return launch_fwd_wide_f32(p, norm, grid, block, groups, st);
+    case GRETA_DT_F16: return launch_fwd_wide_f16(p, norm, grid, block, groups, st);
+    default: return launch_fwd_wide_bf16(p, norm, grid, block, groups, st);
+  }
+}
+
 long long cdiv(long long a, long long b) { return (a + b - 1) / b; }
 
 // Built-in CTA shapes per launch path: {threads along channels (tx), token
@@ -110,21 +122,44 @@ long long cdiv(long long a, long long b) { return (a + b - 1) / b; }
 struct Shape {
   int tx, ty, L;
 };
-constexpr int kPaths = 6;
+enum Path { kPathFwd = 0, kPathBwd, kPathInference, kPathDecodeRows, kPathPackedPrefill, kPathPackedDecode, kPaths };
 constexpr Shape kDefaultShape[kPaths] = {
-    {32, 4, 16},   // GRETA_PATH_FWD
-    {32, 4, 32},   // GRETA_PATH_BWD
-    {32, 4, 16},   // GRETA_PATH_INFERENCE
-    {128, 1, 1},   // GRETA_PATH_DECODE_ROWS
-    {32, 2, 8},    // GRETA_PATH_PACKED_PREFILL
-    {128, 1, 8},   // GRETA_PATH_PACKED_DECODE
+    {32, 4, 16},   // training forward
+    {32, 4, 32},   // training backward
+    {32, 4, 16},   // HF inference from context
+    {128, 1, 1},   // HF decode rows
+    {32, 2, 8},    // packed batches with more than 2 tokens per request
+    {128, 1, 8},   // packed batches with at most 2 tokens per request
 };
-Shape g_override[kPaths] = {};
+
+// Per-call launch choices (greta_dynconv_options); the library keeps no
+// process-wide settings.
+struct Opts {
+  bool reg = false;    // register-staged kernels only
+  Shape shape{0, 0, 0};  // register-kernel CTA shape (tx == 0: built-in)
+  int wait_log2 = 0;   // pipeline wait bound of the row-streaming kernels
+  int withhold = 0;    // test hook of the row-streaming forward
+};
+
+// GRETA_OK and the parsed options, or GRETA_ERR_INVALID_ARG for a bad struct.
+int parse_opts(const greta_dynconv_options* o, Opts& out) {
+  out = Opts{};
+  if (o == nullptr) return GRETA_OK;
+  if (o->size != (int)sizeof(greta_dynconv_options)) return GRETA_ERR_INVALID_ARG;
+  out.reg = o->register_path != 0;
+  if (o->block_x > 0 && o->block_y > 0 && o->tokens > 0) {
+    if (o->block_x % 32 != 0 || o->block_x * o->block_y > 256) return GRETA_ERR_INVALID_ARG;
+    out.shape = Shape{o->block_x, o->block_y, o->tokens};
+  }
+  if (o->wait_limit_log2 != 0 && (o->wait_limit_log2 < 8 || o->wait_limit_log2 > 24)) return GRETA_ERR_INVALID_ARG;
+  out.wait_log2 = o->wait_limit_log2;
+  out.withhold = o->test_withhold_release != 0 ? 1 : 0;
+  return GRETA_OK;
+}
 
 // ---------------------------------------------------------------------------
 // TMA forward (dynconv_fwd_tma.cuh): applicability and shared-memory plan
 // ---------------------------------------------------------------------------
-bool g_tma_enabled = true;
 
 int num_sms() {
   int dev = 0;
@@ -162,8 +197,10 @@ int64_t slice_channels(int64_t D, int64_t max_c) {
 // 16-byte aligned tensors and copies, DS / SD state, at most kMaxSeqsTma
 // sequences, and room for at least two token rows in flight. Returns -1 when
 // it does not.
-int try_rows_fwd(int dtype, RowsParams p, bool gate, int norm, void* stream) {
-  if (!g_tma_enabled) return -1;
+int try_rows_fwd(int dtype, RowsParams p, bool gate, int norm, void* stream, const Opts& o) {
+  if (o.reg) return -1;
+  p.wait_log2 = o.wait_log2;
+  p.withhold = o.withhold;
   const int es = esize(dtype);
   const int64_t D = p.D, W = p.W, G = p.G, DC = D / G;
   if (D % 256 != 0 || W > kMaxWGeneric) return -1;
@@ -254,8 +291,9 @@ cudaError_t run_bwd_rows(int dtype, const BwdRowsParams& p, int norm, int gv, di
 // W <= kMaxWBwdRows, 16-byte aligned tensors and copies, at most kMaxSeqsTma
 // sequences, and room for two stages of token rows (x, filters, dout, gate,
 // saved pre-norm output). Returns -1 when it does not.
-int try_rows_bwd(int dtype, BwdRowsParams p, int norm, void* stream) {
-  if (!g_tma_enabled) return -1;
+int try_rows_bwd(int dtype, BwdRowsParams p, int norm, void* stream, const Opts& o) {
+  if (o.reg) return -1;
+  p.wait_log2 = o.wait_log2;
   const int es = esize(dtype);
   const int64_t D = p.D, W = p.W, G = p.G, DC = D / G;
   if (D % 256 != 0 || W > kMaxWBwdRows) return -1;
@@ -322,8 +360,8 @@ int try_rows_bwd(int dtype, BwdRowsParams p, int norm, void* stream) {
 
 // A run must cover the W-1 history positions: a request's old slot taps are
 // then only read by row 0 of its first chunk.
-Shape shape_for(int path, int H) {
-  Shape s = g_override[path].tx > 0 ? g_override[path] : kDefaultShape[path];
+Shape shape_for(int path, int H, const Opts& o) {
+  Shape s = o.shape.tx > 0 ? o.shape : kDefaultShape[path];
   if (s.L < H) s.L = H;
   if (s.L < 1) s.L = 1;
   return s;
@@ -333,10 +371,14 @@ Shape shape_for(int path, int H) {
 
 extern "C" {
 
-int greta_dynconv_fwd(int dtype, const void* x, const void* w, const void* gate, void* y, void* yr,
-                      const void* cu_seqlens, int cu_seqlens_int64, int64_t num_seqs, int64_t T,
-                      int64_t D, int64_t W, int64_t G, int norm, float eps, void* stream) {
-  int rc = check_common(dtype, D, W, G, norm);
+int greta_dynconv_fwd_ex(int dtype, const void* x, const void* w, const void* gate, void* y, void* yr,
+                         const void* cu_seqlens, int cu_seqlens_int64, int64_t num_seqs, int64_t T,
+                         int64_t D, int64_t W, int64_t G, int norm, float eps, void* stream,
+                         const greta_dynconv_options* opt) {
+  Opts o;
+  int rc = parse_opts(opt, o);
+  if (rc) return rc;
+  rc = check_common(dtype, D, W, G, norm);
   if (rc) return rc;
   if (T < 0 || (cu_seqlens && num_seqs < 0)) return GRETA_ERR_INVALID_ARG;
   if (T == 0 || (cu_seqlens && num_seqs == 0)) return GRETA_OK;  // empty tensors may have null pointers
@@ -351,10 +393,10 @@ int greta_dynconv_fwd(int dtype, const void* x, const void* w, const void* gate,
     tp.nseq = cu_seqlens ? num_seqs : 1;
     tp.T = T; tp.U = T; tp.D = (int)D; tp.W = (int)W; tp.G = (int)G;
     tp.eps = eps;
-    const int r = try_rows_fwd(dtype, tp, gate != nullptr, norm, stream);
+    const int r = try_rows_fwd(dtype, tp, gate != nullptr, norm, stream, o);
     if (r >= 0) return r;
   }
-  const Shape sh = shape_for(GRETA_PATH_FWD, (int)W - 1);
+  const Shape sh = shape_for(kPathFwd, (int)W - 1, o);
   FwdParams p{};
   p.x = x; p.w = w; p.g = gate; p.y = y; p.yr = norm != GRETA_NORM_NONE ? yr : nullptr;
   p.starts = cu_seqlens; p.starts_i64 = cu_seqlens_int64 ? 1 : 0;
@@ -368,11 +410,14 @@ int greta_dynconv_fwd(int dtype, const void* x, const void* w, const void* gate,
   return finish(run_fwd(dtype, p, nv, norm, make_shape(chunks, D, nv, sh.tx, sh.ty), stream));
 }
 
-int greta_dynconv_bwd(int dtype, const void* x, const void* w, const void* gate, const void* yr,
-                      const void* dout, void* dx, void* dw, void* dg, const void* cu_seqlens,
-                      int cu_seqlens_int64, int64_t num_seqs, int64_t T, int64_t D, int64_t W,
-                      int64_t G, int norm, float eps, void* stream) {
-  int rc = check_common(dtype, D, W, G, norm);
+int greta_dynconv_bwd_ex(int dtype, const void* x, const void* w, const void* gate, const void* yr,
+                         const void* dout, void* dx, void* dw, void* dg, const void* cu_seqlens,
+                         int cu_seqlens_int64, int64_t num_seqs, int64_t T, int64_t D, int64_t W,
+                         int64_t G, int norm, float eps, void* stream, const greta_dynconv_options* opt) {
+  Opts o;
+  int rc = parse_opts(opt, o);
+  if (rc) return rc;
+  rc = check_common(dtype, D, W, G, norm);
   if (rc) return rc;
   if (norm == GRETA_NORM_STABLE) return GRETA_ERR_UNSUPPORTED;
   if (T < 0 || (cu_seqlens && num_seqs < 0)) return GRETA_ERR_INVALID_ARG;
@@ -392,10 +437,10 @@ int greta_dynconv_bwd(int dtype, const void* x, const void* w, const void* gate,
     tp.nseq = cu_seqlens ? num_seqs : 1;
     tp.T = T; tp.D = (int)D; tp.W = (int)W; tp.G = (int)G;
     tp.eps = eps;
-    const int r = try_rows_bwd(dtype, tp, norm, stream);
+    const int r = try_rows_bwd(dtype, tp, norm, stream, o);
     if (r >= 0) return r;
   }
-  const Shape sh = shape_for(GRETA_PATH_BWD, (int)W - 1);
+  const Shape sh = shape_for(kPathBwd, (int)W - 1, o);
   BwdParams p{};
   p.x = x; p.w = w; p.g = gate; p.yr = norm != GRETA_NORM_NONE ? yr : nullptr; p.dout = dout;
   p.dx = dx; p.dw = dw; p.dg = dg;
@@ -410,10 +455,13 @@ int greta_dynconv_bwd(int dtype, const void* x, const void* w, const void* gate,
   return finish(run_bwd(dtype, p, nv, norm, make_shape(chunks, D, nv, sh.tx, sh.ty), stream));
 }
 
-int greta_dynconv_inference(int dtype, const void* context, const void* w, const void* gate, void* y,
-                            int64_t B, int64_t Q, int64_t D, int64_t W, int64_t G, int norm, float eps,
-                            void* stream) {
-  int rc = check_common(dtype, D, W, G, norm);
+int greta_dynconv_inference_ex(int dtype, const void* context, const void* w, const void* gate, void* y,
+                               int64_t B, int64_t Q, int64_t D, int64_t W, int64_t G, int norm, float eps,
+                               void* stream, const greta_dynconv_options* opt) {
+  Opts o;
+  int rc = parse_opts(opt, o);
+  if (rc) return rc;
+  rc = check_common(dtype, D, W, G, norm);
   if (rc) return rc;
   if (B < 0 || Q < 0) return GRETA_ERR_INVALID_ARG;
   if (B == 0 || Q == 0) return GRETA_OK;  // empty tensors may have null pointers
@@ -427,10 +475,10 @@ int greta_dynconv_inference(int dtype, const void* context, const void* w, const
     tp.nseq = B;
     tp.T = Q; tp.U = B * Q; tp.D = (int)D; tp.W = (int)W; tp.G = (int)G;
     tp.eps = eps;
-    const int r = try_rows_fwd(dtype, tp, gate != nullptr, norm, stream);
+    const int r = try_rows_fwd(dtype, tp, gate != nullptr, norm, stream, o);
     if (r >= 0) return r;
   }
-  const Shape sh = shape_for(GRETA_PATH_INFERENCE, (int)W - 1);
+  const Shape sh = shape_for(kPathInference, (int)W - 1, o);
   FwdParams p{};
   p.x = context; p.w = w; p.g = gate; p.y = y; p.yr = nullptr;
   p.mode = kModeContext;
@@ -443,10 +491,13 @@ int greta_dynconv_inference(int dtype, const void* context, const void* w, const
   return finish(run_fwd(dtype, p, nv, norm, make_shape(chunks, D, nv, sh.tx, sh.ty), stream));
 }
 
-int greta_dynconv_decode_rows(int dtype, const void* x, const void* w, const void* gate, void* conv_state,
-                              void* y, int64_t B, int64_t D, int64_t W, int64_t G, int norm, float eps,
-                              void* stream) {
-  int rc = check_common(dtype, D, W, G, norm);
+int greta_dynconv_decode_rows_ex(int dtype, const void* x, const void* w, const void* gate, void* conv_state,
+                                 void* y, int64_t B, int64_t D, int64_t W, int64_t G, int norm, float eps,
+                                 void* stream, const greta_dynconv_options* opt) {
+  Opts o;
+  int rc = parse_opts(opt, o);
+  if (rc) return rc;
+  rc = check_common(dtype, D, W, G, norm);
   if (rc) return rc;
   if (B < 0 || W < 2) return GRETA_ERR_INVALID_ARG;
   if (B == 0) return GRETA_OK;  // empty tensors may have null pointers
@@ -466,18 +517,21 @@ int greta_dynconv_decode_rows(int dtype, const void* x, const void* w, const voi
   p.s_slot = D * H; p.s_d = H; p.s_h = 1; p.num_slots = B;
   p.st_layout = (nv == kVec && aligned(conv_state, (int64_t)kVec * es)) ? kStDS : kStGeneric;
   p.eps = eps;
-  const Shape sh = shape_for(GRETA_PATH_DECODE_ROWS, H);
+  const Shape sh = shape_for(kPathDecodeRows, H, o);
   if (nv == kVec && (W == 4 || W == 7) && p.st_layout == kStDS && sh.tx <= 128)
     return finish(run_fwd_decode(dtype, p, norm, make_shape(B, D, nv, sh.tx, 1), stream));
   return finish(run_fwd(dtype, p, nv, norm, make_shape(B, D, nv, sh.tx, 1), stream));
 }
 
-int greta_dynconv_packed_state(int dtype, const void* x, const void* w, const void* gate, void* y,
-                               void* state, int64_t num_slots, int64_t s_slot, int64_t s_d, int64_t s_h,
-                               const int32_t* starts, const int32_t* slots, const int8_t* has_initial,
-                               int64_t num_reqs, int64_t T, int64_t D, int64_t W, int64_t G, int norm,
-                               float eps, int32_t* error_flags, void* stream) {
-  int rc = check_common(dtype, D, W, G, norm);
+int greta_dynconv_packed_state_ex(int dtype, const void* x, const void* w, const void* gate, void* y,
+                                  void* state, int64_t num_slots, int64_t s_slot, int64_t s_d, int64_t s_h,
+                                  const int32_t* starts, const int32_t* slots, const int8_t* has_initial,
+                                  int64_t num_reqs, int64_t T, int64_t D, int64_t W, int64_t G, int norm,
+                                  float eps, int32_t* error_flags, void* stream, const greta_dynconv_options* opt) {
+  Opts o;
+  int rc = parse_opts(opt, o);
+  if (rc) return rc;
+  rc = check_common(dtype, D, W, G, norm, D);
   if (rc) return rc;
   const int H = (int)W - 1;
   if (T < 0 || num_reqs < 0 || num_slots < 0) return GRETA_ERR_INVALID_ARG;
@@ -488,7 +542,7 @@ int greta_dynconv_packed_state(int dtype, const void* x, const void* w, const vo
   if (nv == 0) return GRETA_ERR_ALIGNMENT;
   const int es = esize(dtype);
   const bool decode_like = T <= 2 * num_reqs;
-  const Shape sh = shape_for(decode_like ? GRETA_PATH_PACKED_DECODE : GRETA_PATH_PACKED_PREFILL, H);
+  const Shape sh = shape_for(decode_like ? kPathPackedDecode : kPathPackedPrefill, H, o);
   FwdParams p{};
   p.x = x; p.w = w; p.g = gate; p.y = y; p.yr = nullptr;
   p.starts = starts; p.starts_i64 = 0;
@@ -516,6 +570,18 @@ int greta_dynconv_packed_state(int dtype, const void* x, const void* w, const vo
     p.state = nullptr;
     p.num_slots = 0;
   }
+  if (G > 256) {
+    // groups wider than one warp's 256 channels: each CTA owns one whole
+    // group of a chunk of kWideChunk tokens (dynconv_fwd_wide.cuh)
+    if (nv != kVec) return GRETA_ERR_ALIGNMENT;
+    p.L = p.chunk = kWideChunk;
+    const long long groups = D / G;
+    const long long rows = cdiv(T, p.chunk) + num_reqs;
+    if (rows * groups > INT_MAX) return GRETA_ERR_INVALID_ARG;
+    const int threads = (int)(G / kVec < kWideThreads ? G / kVec : kWideThreads);
+    return finish(run_fwd_wide(dtype, p, norm, dim3((unsigned)(rows * groups)), dim3((unsigned)threads), (int)groups,
+                               stream));
+  }
   if (!decode_like && nv == kVec) {
     RowsParams tp{};
     tp.x = x; tp.w = w; tp.g = gate; tp.y = y; tp.yr = nullptr;
@@ -526,7 +592,7 @@ int greta_dynconv_packed_state(int dtype, const void* x, const void* w, const vo
     tp.state = p.state; tp.s_slot = p.s_slot; tp.s_d = p.s_d; tp.s_h = p.s_h; tp.num_slots = p.num_slots;
     tp.st_layout = p.st_layout; tp.slots = slots; tp.initial = p.initial; tp.err = error_flags;
     tp.eps = eps;
-    const int r = try_rows_fwd(dtype, tp, gate != nullptr, norm, stream);
+    const int r = try_rows_fwd(dtype, tp, gate != nullptr, norm, stream, o);
     if (r >= 0) return r;
   }
   if (decode_like && nv == kVec && (W == 4 || W == 7) && sh.ty == 1 && sh.tx <= 128 && T < INT_MAX &&
@@ -543,9 +609,37 @@ int greta_dynconv_packed_state(int dtype, const void* x, const void* w, const vo
   return finish(run_fwd(dtype, p, nv, norm, make_shape(chunks, D, nv, sh.tx, sh.ty), stream));
 }
 
-int greta_dynconv_set_tma(int enable) {
-  g_tma_enabled = enable != 0;
-  return GRETA_OK;
+int greta_dynconv_fwd(int dtype, const void* x, const void* w, const void* gate, void* y, void* yr,
+                      const void* cu_seqlens, int cu_seqlens_int64, int64_t num_seqs, int64_t T, int64_t D,
+                      int64_t W, int64_t G, int norm, float eps, void* stream) {
+  return greta_dynconv_fwd_ex(dtype, x, w, gate, y, yr, cu_seqlens, cu_seqlens_int64, num_seqs, T, D, W, G, norm,
+                              eps, stream, nullptr);
+}
+
+int greta_dynconv_bwd(int dtype, const void* x, const void* w, const void* gate, const void* yr, const void* dout,
+                      void* dx, void* dw, void* dg, const void* cu_seqlens, int cu_seqlens_int64, int64_t num_seqs,
+                      int64_t T, int64_t D, int64_t W, int64_t G, int norm, float eps, void* stream) {
+  return greta_dynconv_bwd_ex(dtype, x, w, gate, yr, dout, dx, dw, dg, cu_seqlens, cu_seqlens_int64, num_seqs, T, D,
+                              W, G, norm, eps, stream, nullptr);
+}
+
+int greta_dynconv_inference(int dtype, const void* context, const void* w, const void* gate, void* y, int64_t B,
+                            int64_t Q, int64_t D, int64_t W, int64_t G, int norm, float eps, void* stream) {
+  return greta_dynconv_inference_ex(dtype, context, w, gate, y, B, Q, D, W, G, norm, eps, stream, nullptr);
+}
+
+int greta_dynconv_decode_rows(int dtype, const void* x, const void* w, const void* gate, void* conv_state, void* y,
+                              int64_t B, int64_t D, int64_t W, int64_t G, int norm, float eps, void* stream) {
+  return greta_dynconv_decode_rows_ex(dtype, x, w, gate, conv_state, y, B, D, W, G, norm, eps, stream, nullptr);
+}
+
+int greta_dynconv_packed_state(int dtype, const void* x, const void* w, const void* gate, void* y, void* state,
+                               int64_t num_slots, int64_t s_slot, int64_t s_d, int64_t s_h, const int32_t* starts,
+                               const int32_t* slots, const int8_t* has_initial, int64_t num_reqs, int64_t T,
+                               int64_t D, int64_t W, int64_t G, int norm, float eps, int32_t* error_flags,
+                               void* stream) {
+  return greta_dynconv_packed_state_ex(dtype, x, w, gate, y, state, num_slots, s_slot, s_d, s_h, starts, slots,
+                                       has_initial, num_reqs, T, D, W, G, norm, eps, error_flags, stream, nullptr);
 }
 
 int greta_dynconv_device_errors(int clear) {
@@ -560,20 +654,8 @@ int greta_dynconv_device_errors(int clear) {
   return all;
 }
 
-int greta_dynconv_set_launch_shape(int path, int block_x, int block_y, int tokens) {
-  if (path < 0 || path >= kPaths) return GRETA_ERR_INVALID_ARG;
-  if (block_x <= 0 || block_y <= 0 || tokens <= 0) {
-    g_override[path] = Shape{0, 0, 0};
-    return GRETA_OK;
-  }
-  if (block_x % 32 != 0 || block_x * block_y > 256) return GRETA_ERR_INVALID_ARG;
-  if (path == GRETA_PATH_DECODE_ROWS && block_y != 1) return GRETA_ERR_INVALID_ARG;
-  g_override[path] = Shape{block_x, block_y, tokens};
-  return GRETA_OK;
-}
-
 int greta_dynconv_supports(int64_t group_size, int64_t channels) {
-  return (is_pow2(group_size) && group_size <= 256 && channels > 0 && channels % group_size == 0) ? 1 : 0;
+  return (is_pow2(group_size) && channels > 0 && channels % group_size == 0) ? 1 : 0;
 }
 
 const char* greta_dynconv_status_string(int status) {

@@ -308,10 +308,12 @@ __device__ __forceinline__ void group_max_sum(const float (&a)[NV], const float 
 // The overflow-safe group RMS norm, given the group max of |y| (mx) and the
 // group sum of y^2 (ss). Its form s * sqrt(mean((y/s)^2) + eps/s^2), with
 // s = max(max|y|, 1), equals sqrt(mean(y^2) + eps): while every group of the
-// warp has max|y| <= 2^60 (squares, and their sums over at most 256 channels,
-// stay finite) that is what is computed; otherwise (or for a NaN) the warp
-// takes the rescaled two-pass form. For max|y| <= 1 both are the same
-// arithmetic. Must be called by all 32 lanes.
+// warp has max|y| < 2^60 that is what is computed; otherwise (or for a NaN)
+// the warp takes the rescaled two-pass form. The bound is strict: each square
+// is then below 2^120, and a rounded sum of at most 256 of them stays below
+// 256 * 2^120 = 2^128, i.e. finite, whereas 256 squares of exactly 2^60 sum
+// to 2^128 = inf. For max|y| <= 1 both forms are the same arithmetic. Must be
+// called by all 32 lanes.
 template <int NV, int GV>
 __device__ __forceinline__ void stable_finish(float (&acc)[NV], float (&mx)[GV], float (&ss)[GV], int G, int lpg,
                                               float eps) {
@@ -319,7 +321,7 @@ __device__ __forceinline__ void stable_finish(float (&acc)[NV], float (&mx)[GV],
   const float inv_g = 1.f / (float)G;  // G is a power of two: exact
   bool big = false;
 #pragma unroll
-  for (int gi = 0; gi < GV; ++gi) big = big || !(mx[gi] <= 0x1p60f);
+  for (int gi = 0; gi < GV; ++gi) big = big || !(mx[gi] < 0x1p60f);
   if (__any_sync(0xffffffffu, big)) {
 #pragma unroll
     for (int gi = 0; gi < GV; ++gi) mx[gi] = __frcp_rn(fmaxf(mx[gi], 1.f));  // 1 / s, exact for s up to FLT_MAX

@@ -64,6 +64,8 @@ struct RowsParams {
   const signed char* initial;
   int* err;  // slot-range error bits (may be null)
   float eps;
+  int wait_log2;  // pipeline wait bound: 2^wait_log2 polls (0 = default)
+  int withhold;   // test hook: consumer warp 0 of CTA 0 keeps its first stage
   // shared-memory layout (bytes from the dynamic base): sequence offsets
   // [nseq + 1] (int64), request slots [nseq] (int32) and flags [nseq] (int8),
   // then the stages
@@ -193,6 +195,7 @@ __global__ void __launch_bounds__(32 + fwd_rows_max_channels(WT) / kVec, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nconsw = (int)(blockDim.x >> 5) - 1;  // consumer warps
   const int S = p.stages;
+  const unsigned wlimit = wait_limit(p.wait_log2);
 
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ __align__(8) unsigned long long bars[2 * kMaxStages];
@@ -342,7 +345,7 @@ __global__ void __launch_bounds__(32 + fwd_rows_max_channels(WT) / kVec, 1)
     int cq = q0;
     int i = 0;
     for (long long t0 = u0; t0 < u1; t0 += p.BT, ++i) {
-      if (i >= S && !mbar_wait(empty0 + 8 * s, par ^ 1u)) {
+      if (i >= S && !mbar_wait(empty0 + 8 * s, par ^ 1u, wlimit)) {
         atomicOr(&g_tma_errors, kErrTimeout);
         return;
       }
@@ -480,7 +483,7 @@ __global__ void __launch_bounds__(32 + fwd_rows_max_channels(WT) / kVec, 1)
   long long cb = b0;  // CONTEXT: batch row and position of the current token
   int cq = q0;
   for (long long t0 = u0; t0 < u1; t0 += p.BT) {
-    if (!mbar_wait(full0 + 8 * s, par)) {
+    if (!mbar_wait(full0 + 8 * s, par, wlimit)) {
       if (lane == 0) atomicOr(&g_tma_errors, kErrTimeout);
       return;
     }
@@ -644,7 +647,10 @@ __global__ void __launch_bounds__(32 + fwd_rows_max_channels(WT) / kVec, 1)
       yp += D;
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive(empty0 + 8 * cur_s);
+    // (test hook: consumer warp 0 of CTA 0 keeps the first stage it used, so
+    // the producer's refill of it waits until its bound runs out)
+    const bool keep = p.withhold != 0 && blockIdx.x == 0 && warp == 1 && t0 == u0;
+    if (lane == 0 && !keep) mbar_arrive(empty0 + 8 * cur_s);
   }
 }
 

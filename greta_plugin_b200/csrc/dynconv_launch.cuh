@@ -187,6 +187,10 @@ cudaError_t launch_fwd_rows_bf16(const RowsParams&, int, int, dim3, dim3, size_t
 cudaError_t launch_fwd_decode_f32(const FwdParams&, int, int, const LaunchShape&, cudaStream_t);
 cudaError_t launch_fwd_decode_f16(const FwdParams&, int, int, const LaunchShape&, cudaStream_t);
 cudaError_t launch_fwd_decode_bf16(const FwdParams&, int, int, const LaunchShape&, cudaStream_t);
+// packed forward for groups wider than 256 channels (dynconv_fwd_decode_<dtype>.cu)
+cudaError_t launch_fwd_wide_f32(const FwdParams&, int, dim3, dim3, int, cudaStream_t);
+cudaError_t launch_fwd_wide_f16(const FwdParams&, int, dim3, dim3, int, cudaStream_t);
+cudaError_t launch_fwd_wide_bf16(const FwdParams&, int, dim3, dim3, int, cudaStream_t);
 int device_errors_f32(bool clear);
 int device_errors_f16(bool clear);
 int device_errors_bf16(bool clear);

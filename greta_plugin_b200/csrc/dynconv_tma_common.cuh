@@ -53,9 +53,16 @@ __device__ __forceinline__ void mbar_arrive(unsigned bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(bar) : "memory");
 }
 
-// Bounded wait for the phase with the given parity; false on timeout (~1 s).
-__device__ __forceinline__ bool mbar_wait(unsigned bar, unsigned parity) {
-  for (unsigned it = 0; it < (1u << 24); ++it) {
+// Polls of a pipeline wait: 2^24 (about a second) unless a launch option
+// asks for fewer (tests that make a wait run out).
+__host__ __device__ constexpr unsigned wait_limit(int log2) {
+  return (log2 >= 8 && log2 <= 24) ? (1u << log2) : (1u << 24);
+}
+
+// Bounded wait for the phase with the given parity; false once `limit`
+// polls have passed.
+__device__ __forceinline__ bool mbar_wait(unsigned bar, unsigned parity, unsigned limit) {
+  for (unsigned it = 0; it < limit; ++it) {
     unsigned done;
     asm volatile(
         "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"

@@ -199,10 +199,10 @@ def dynconv_fwd(
     yr = torch.empty_like(x) if (norm and save_pre) else None
     cu, cu64, nseq = _cu(cu_seqlens, x.device)
     with custom_device_ctx(x.device.index):
-        st = _capi.lib().greta_dynconv_fwd(
+        st = _capi.lib().greta_dynconv_fwd_ex(
             _capi.dtype_code(x), _capi.ptr(x), _capi.ptr(wk), _capi.ptr(gk), _capi.ptr(y), _capi.ptr(yr),
             _capi.ptr(cu), cu64, nseq, T, D, W, group_size, _capi.NORM_PLAIN if norm else _capi.NORM_NONE,
-            float(eps), _capi.stream_of(x))
+            float(eps), _capi.stream_of(x), _capi.options())
     _capi.check("greta_dynconv_fwd", st)
     return y.view(shape_x), yr, (BT if BT is not None else _TRAIN_CHUNK), None
 
@@ -241,10 +241,11 @@ def dynconv_bwd(
     dg = torch.empty_like(gk) if gk is not None else None
     cu, cu64, nseq = _cu(cu_seqlens, x.device)
     with custom_device_ctx(x.device.index):
-        st = _capi.lib().greta_dynconv_bwd(
+        st = _capi.lib().greta_dynconv_bwd_ex(
             _capi.dtype_code(x), _capi.ptr(x), _capi.ptr(wk), _capi.ptr(gk), _capi.ptr(yk if norm else None),
             _capi.ptr(dk), _capi.ptr(dx), _capi.ptr(dw), _capi.ptr(dg), _capi.ptr(cu), cu64, nseq, T, D, W,
-            group_size, _capi.NORM_PLAIN if norm else _capi.NORM_NONE, float(eps), _capi.stream_of(x))
+            group_size, _capi.NORM_PLAIN if norm else _capi.NORM_NONE, float(eps), _capi.stream_of(x),
+            _capi.options())
     _capi.check("greta_dynconv_bwd", st)
     if dw.dtype != weight.dtype:
         dw = dw.to(weight.dtype)
@@ -338,10 +339,10 @@ def dynamic_causal_conv1d_inference(
     wk, gk = _as(weight, context.dtype), _as(gate, context.dtype)
     y = context.new_empty((B, Q, D))
     with custom_device_ctx(context.device.index):
-        st = _capi.lib().greta_dynconv_inference(
+        st = _capi.lib().greta_dynconv_inference_ex(
             _capi.dtype_code(context), _capi.ptr(context), _capi.ptr(wk), _capi.ptr(gk), _capi.ptr(y), B, Q, D, W,
             group_size, _capi.NORM_PLAIN if norm else _capi.NORM_NONE, float(norm_eps),
-            _capi.stream_of(context))
+            _capi.stream_of(context), _capi.options())
     _capi.check("greta_dynconv_inference", st)
     return y
 
@@ -375,10 +376,10 @@ def dynamic_causal_conv1d_decode(
     wk, gk = _as(weight, x.dtype), _as(gate, x.dtype)
     y = torch.empty_like(x)
     with custom_device_ctx(x.device.index):
-        st = _capi.lib().greta_dynconv_decode_rows(
+        st = _capi.lib().greta_dynconv_decode_rows_ex(
             _capi.dtype_code(x), _capi.ptr(x), _capi.ptr(wk), _capi.ptr(gk), _capi.ptr(conv_state), _capi.ptr(y),
             B, D, W, group_size, _capi.NORM_PLAIN if norm else _capi.NORM_NONE, float(norm_eps),
-            _capi.stream_of(x))
+            _capi.stream_of(x), _capi.options())
     _capi.check("greta_dynconv_decode_rows", st)
     return y
 

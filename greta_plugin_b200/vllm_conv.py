@@ -22,14 +22,11 @@ import torch
 
 from . import _capi
 
-MAX_GROUP = 256
-
-
 def supports(group_size: int, channels: int) -> bool:
-    """The kernels tile channels by whole norm groups of a power-of-two size
-    (one group within one warp, so G <= 256)."""
-    return (group_size > 0 and group_size & (group_size - 1) == 0 and channels % group_size == 0
-            and group_size <= MAX_GROUP)
+    """The reference's rule (greta_vllm/triton_conv.py:119-121): a power-of-two
+    group size dividing the channels. Groups of up to 256 channels run within
+    one warp; wider ones on a kernel that gives each CTA one whole group."""
+    return group_size > 0 and group_size & (group_size - 1) == 0 and channels % group_size == 0
 
 
 def _launch(x, weights, gate, state, starts, slots, has_initial, group_size, norm, eps, out, flags):
@@ -60,11 +57,12 @@ def _launch(x, weights, gate, state, starts, slots, has_initial, group_size, nor
     has_initial = has_initial.to(device=x.device, dtype=torch.int8).reshape(-1).contiguous()
     s_slot, s_d, s_h = state.stride()
     with torch.cuda.device(x.device.index):
-        st = _capi.lib().greta_dynconv_packed_state(
+        st = _capi.lib().greta_dynconv_packed_state_ex(
             _capi.dtype_code(x), _capi.ptr(x), _capi.ptr(weights), _capi.ptr(gate), _capi.ptr(out),
             _capi.ptr(state) if state.numel() else None, state.shape[0], s_slot, s_d, s_h, _capi.ptr(starts),
             _capi.ptr(slots), _capi.ptr(has_initial), slots.numel(), tokens, channels, width, group_size,
-            _capi.NORM_STABLE if norm else _capi.NORM_NONE, float(eps), _capi.ptr(flags), _capi.stream_of(x))
+            _capi.NORM_STABLE if norm else _capi.NORM_NONE, float(eps), _capi.ptr(flags), _capi.stream_of(x),
+            _capi.options())
     _capi.check("greta_dynconv_packed_state", st)
     return out
 
@@ -83,16 +81,20 @@ def packed_dynamic_conv_triton(x, weights, gate, state, starts, slots, has_initi
 
 def packed_dynamic_conv_checked(x, weights, gate, state, starts, slots, has_initial, group_size, norm=True,
                                 eps=1e-6, out=None):
-    """packed_dynamic_conv_triton plus a device check of the slot indices.
+    """packed_dynamic_conv_triton plus device checks.
 
     Slots >= state.shape[0] are skipped by the kernel (no read, no write-back)
-    and reported here as IndexError. The check synchronises the stream, so it
+    and reported here as IndexError. A pipeline wait of a row-streaming kernel
+    that ran out (the kernel then returns with part of `out` unwritten) is
+    reported as GretaKernelError. The checks synchronise the device, so this
     is for debugging and tests, not for the serving loop.
     """
     flags = torch.zeros(1, dtype=torch.int32, device=x.device)
     out = _launch(x, weights, gate, state, starts, slots, has_initial, group_size, norm, eps, out, flags)
     if int(flags.item()) & 1:
         raise IndexError(f"a cache slot index is >= the number of cache slots ({state.shape[0]})")
+    with torch.cuda.device(x.device.index):
+        _capi.check_device_errors("packed_dynamic_conv_checked")
     return out
 
 

@@ -24,8 +24,14 @@
  *     issued while a stream is being captured into a CUDA graph.
  *   - Return value: GRETA_OK or one of the GRETA_ERR_* codes below. On an
  *     argument error nothing is launched.
- *   - The group size G must be a power of two dividing D, with G <= 256.
- *     The kernel size W must be in [1, 16] (the decode entry points need W >= 2).
+ *   - The group size G must be a power of two dividing D, with G <= 256,
+ *     except for greta_dynconv_packed_state, which takes any power of two
+ *     dividing D (as the reference's vLLM path does). The kernel size W must
+ *     be in [1, 16] (the decode entry points need W >= 2).
+ *   - Every entry point has an `_ex` form with a trailing
+ *     `const greta_dynconv_options*` (NULL = the plain form's behaviour):
+ *     per-call launch choices for tests and tuning sweeps. The library keeps
+ *     no process-wide settings.
  *   - Weights are compact and tap-major: w[t, k, f] with f = d / G.
  */
 #ifndef GRETA_DYNCONV_H
@@ -58,7 +64,7 @@ extern "C" {
 /* status codes */
 #define GRETA_OK 0
 #define GRETA_ERR_INVALID_ARG 1 /* null pointer, negative size, shape mismatch */
-#define GRETA_ERR_UNSUPPORTED 2 /* G not a power of two / > 256, W out of range, dtype */
+#define GRETA_ERR_UNSUPPORTED 2 /* G not a power of two (or > 256 where noted), W out of range, dtype */
 #define GRETA_ERR_ALIGNMENT 3   /* a pointer or stride breaks the vector-path alignment */
 #define GRETA_ERR_LAUNCH 4      /* the CUDA launch itself failed */
 
@@ -142,6 +148,8 @@ GRETA_API int greta_dynconv_decode_rows(int dtype, const void* x, const void* w,
  *   has_initial: [num_reqs] int8; 0 = ignore the slot's old contents (zeros)
  *   norm       : GRETA_NORM_NONE, GRETA_NORM_PLAIN or GRETA_NORM_STABLE
  *                (the vLLM plugin uses STABLE)
+ *   G          : any power of two dividing D; groups wider than 256 channels
+ *                run on a kernel that gives each CTA one whole group
  *   error_flags: NULL, or a device int32 that receives OR-ed error bits
  *
  * After the call, each request's slot holds its last W-1 inputs (taken from
@@ -155,43 +163,63 @@ GRETA_API int greta_dynconv_packed_state(int dtype, const void* x, const void* w
                                int64_t num_reqs, int64_t T, int64_t D, int64_t W, int64_t G,
                                int norm, float eps, int32_t* error_flags, void* stream);
 
-/* Launch paths, for greta_dynconv_set_launch_shape. */
-#define GRETA_PATH_FWD 0
-#define GRETA_PATH_BWD 1
-#define GRETA_PATH_INFERENCE 2
-#define GRETA_PATH_DECODE_ROWS 3
-#define GRETA_PATH_PACKED_PREFILL 4 /* packed batches with more than 2 tokens per request */
-#define GRETA_PATH_PACKED_DECODE 5  /* packed batches with at most 2 tokens per request */
-
 /*
- * Tuning knob (no counterpart in the reference, whose Triton kernels are
- * autotuned): overrides the CTA shape of one launch path for the whole
- * process. block_x = threads along channels (multiple of 32), block_y = token
- * runs per CTA, tokens = tokens per run (raised to at least W-1), with
- * block_x * block_y <= 256. Any argument <= 0 restores the built-in shape.
- * Returns GRETA_ERR_INVALID_ARG for an unknown path or a bad shape.
+ * Per-call launch options (no counterpart in the reference, whose Triton
+ * kernels are autotuned). Pass to the `_ex` entry points; NULL, or a zeroed
+ * struct with `size` set, means the built-in choices. Nothing here changes
+ * results beyond floating-point summation order, except the test hooks,
+ * which make a kernel stop early on purpose.
  */
-GRETA_API int greta_dynconv_set_launch_shape(int path, int block_x, int block_y, int tokens);
+typedef struct greta_dynconv_options {
+  int size;          /* sizeof(greta_dynconv_options); other sizes are rejected */
+  int register_path; /* != 0: never use the row-streaming (bulk-copy) kernels; the
+                        register-staged kernels give the same bits */
+  int block_x;       /* register-kernel CTA shape: threads along channels (multiple of 32), */
+  int block_y;       /* token runs per CTA (block_x * block_y <= 256) and */
+  int tokens;        /* tokens per run (raised to at least W-1); any <= 0 = built-in shape */
+  int wait_limit_log2; /* bound of each pipeline (mbarrier) wait in the row-streaming
+                          kernels: 2^n polls, 8 <= n <= 24; 0 = 2^24 (about a second) */
+  int test_withhold_release; /* test hook: != 0 makes consumer warp 0 of CTA 0 of the
+                                row-streaming forward keep its first stage, so that the
+                                producer's bounded wait runs out (device error bit 1, see
+                                greta_dynconv_device_errors); the launch still returns */
+} greta_dynconv_options;
 
-/*
- * Selects the forward implementation for long token streams (no counterpart
- * in the reference): enable != 0 (the default) stages operands through the
- * Tensor Memory Accelerator where the shapes allow it (D a multiple of 256,
- * 16-byte aligned rows, DS/SD state layouts, at most 2048 sequences,
- * prefill-like batches); 0 always uses the register-staged kernels. Both give
- * the same results. Process-wide; returns GRETA_OK.
- */
-GRETA_API int greta_dynconv_set_tma(int enable);
+GRETA_API int greta_dynconv_fwd_ex(int dtype, const void* x, const void* w, const void* gate, void* y,
+                                   void* yr, const void* cu_seqlens, int cu_seqlens_int64,
+                                   int64_t num_seqs, int64_t T, int64_t D, int64_t W, int64_t G,
+                                   int norm, float eps, void* stream, const greta_dynconv_options* opt);
+GRETA_API int greta_dynconv_bwd_ex(int dtype, const void* x, const void* w, const void* gate,
+                                   const void* yr, const void* dout, void* dx, void* dw, void* dg,
+                                   const void* cu_seqlens, int cu_seqlens_int64, int64_t num_seqs,
+                                   int64_t T, int64_t D, int64_t W, int64_t G, int norm, float eps,
+                                   void* stream, const greta_dynconv_options* opt);
+GRETA_API int greta_dynconv_inference_ex(int dtype, const void* context, const void* w, const void* gate,
+                                         void* y, int64_t B, int64_t Q, int64_t D, int64_t W, int64_t G,
+                                         int norm, float eps, void* stream, const greta_dynconv_options* opt);
+GRETA_API int greta_dynconv_decode_rows_ex(int dtype, const void* x, const void* w, const void* gate,
+                                           void* conv_state, void* y, int64_t B, int64_t D, int64_t W,
+                                           int64_t G, int norm, float eps, void* stream,
+                                           const greta_dynconv_options* opt);
+GRETA_API int greta_dynconv_packed_state_ex(int dtype, const void* x, const void* w, const void* gate,
+                                            void* y, void* state, int64_t num_slots, int64_t s_slot,
+                                            int64_t s_d, int64_t s_h, const int32_t* starts,
+                                            const int32_t* slots, const int8_t* has_initial,
+                                            int64_t num_reqs, int64_t T, int64_t D, int64_t W, int64_t G,
+                                            int norm, float eps, int32_t* error_flags, void* stream,
+                                            const greta_dynconv_options* opt);
 
 /*
  * Device-side error bits recorded by earlier kernels of this library on the
- * current device (bit 1: a pipeline wait timed out and the kernel returned
- * early). Synchronises the device; clear != 0 resets the bits. Returns the
- * bits, or -1 when they cannot be read. For debugging and tests.
+ * current device (bit 1, value 2: a pipeline wait of a row-streaming kernel
+ * timed out and the kernel returned early, leaving part of its outputs
+ * unwritten). Synchronises the device; clear != 0 resets the bits. Returns
+ * the bits, or -1 when they cannot be read. For debugging and tests.
  */
 GRETA_API int greta_dynconv_device_errors(int clear);
 
-/* Mirrors supports() in greta_vllm/triton_conv.py:119-121 (plus the G <= 256 limit). */
+/* supports() of greta_vllm/triton_conv.py:119-121: G a power of two dividing
+ * `channels` (the packed entry point's rule). */
 GRETA_API int greta_dynconv_supports(int64_t group_size, int64_t channels);
 
 /* Human-readable text for a status code (static storage). */

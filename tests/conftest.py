@@ -20,6 +20,23 @@ def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: requires a CUDA GPU (B200, sm_100a)")
 
 
+@pytest.fixture(autouse=True)
+def _no_device_errors(request):
+    """After every GPU test: no kernel of the library recorded a device error
+    (a pipeline wait that ran out). Tests that cause one on purpose clear it."""
+    yield
+    if request.node.get_closest_marker("gpu") is None:
+        return
+    import torch
+
+    if not torch.cuda.is_available():
+        return
+    from greta_plugin_b200 import _capi
+
+    bits = _capi.device_errors(clear=True)
+    assert bits == 0, f"a kernel recorded device error bits {bits:#x}"
+
+
 @pytest.fixture(scope="session")
 def golden_dir():
     return GOLDEN
@@ -48,5 +65,19 @@ def f32_to_bf16_bits(a):
     return r
 
 
+# The unmodified reference (Garbo-AI/greta-plugin) as installed into
+# baseline/_ref by `pip install --target baseline/_ref <checkout>`; the
+# GRETA_REFERENCE environment variable may point at another installed copy.
+REFERENCE_DIR = Path(os.environ.get("GRETA_REFERENCE") or (ROOT / "baseline" / "_ref"))
+
+
 def reference_available():
-    return Path(os.environ.get("GRETA_REFERENCE", "/root/reference")).is_dir()
+    return (REFERENCE_DIR / "greta" / "dynamic_conv.py").is_file() and (REFERENCE_DIR / "greta_vllm").is_dir()
+
+
+def import_reference_path():
+    """Put the installed reference on sys.path (tests that use it skip without it)."""
+    if not reference_available():
+        pytest.skip(f"the reference is not installed at {REFERENCE_DIR}")
+    if str(REFERENCE_DIR) not in sys.path:
+        sys.path.insert(0, str(REFERENCE_DIR))

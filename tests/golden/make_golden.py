@@ -31,8 +31,11 @@ OUT = Path(__file__).resolve().parent
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("GRETA_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("GRETA_REFERENCE"),
+                    help="checkout of Garbo-AI/greta-plugin (or set GRETA_REFERENCE)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("pass --reference <checkout of the reference> or set GRETA_REFERENCE")
     os.environ["TRITON_INTERPRET"] = "1"
     sys.path.insert(0, args.reference)
 

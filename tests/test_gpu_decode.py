@@ -17,7 +17,6 @@ from test_gpu_packed import make_batch, run_and_check
 
 pytestmark = pytest.mark.gpu
 
-PACKED_DECODE = 5  # GRETA_PATH_PACKED_DECODE
 
 
 def decode_batch(n_req, n_slots, seed, extra=None):
@@ -79,16 +78,13 @@ def test_decode_kernel_bit_identical_to_register_kernel():
         lengths, slots, init = decode_batch(80, 90, seed=W + G, extra=extra)
         b = make_batch(lengths, slots, init, 96, 1024, W, G, torch.bfloat16, seed=21, gate_on=True)
         outs = []
-        try:
-            for shape in ((0, 0, 0), (256, 1, 8)):
-                _capi.set_launch_shape(PACKED_DECODE, *shape)
+        for shape in ((0, 0, 0), (256, 1, 8)):
+            with _capi.launch_options(block_x=shape[0], block_y=shape[1], tokens=shape[2]):
                 state = b["state"].clone()
                 y = packed_dynamic_conv_triton(b["x"].to(DEV), b["w"].to(DEV), b["gate"].to(DEV), state,
                                                b["starts"].to(DEV), b["slots"].to(DEV), b["init"].to(DEV), G,
                                                norm=True, eps=1e-6)
                 outs.append((y, state))
-        finally:
-            _capi.set_launch_shape(PACKED_DECODE)
         assert torch.equal(outs[0][0].view(torch.int16), outs[1][0].view(torch.int16))
         assert torch.equal(outs[0][1].view(torch.int16), outs[1][1].view(torch.int16))
 

@@ -144,13 +144,10 @@ def test_decode_rows_kernels_bit_identical(W, G, norm, gate_on):
     gate = rand(g, B, D).to(DEV) if gate_on else None
     state0 = rand(g, B, D, W - 1).to(DEV)
     outs = []
-    try:
-        for shape in ((0, 0, 0), (256, 1, 1)):
-            _capi.set_launch_shape(3, *shape)  # GRETA_PATH_DECODE_ROWS
+    for shape in ((0, 0, 0), (256, 1, 1)):
+        with _capi.launch_options(block_x=shape[0], block_y=shape[1], tokens=shape[2]):
             st = state0.clone()
             y = dynamic_causal_conv1d_decode(x, w, st, gate, G, norm)
             outs.append((y, st))
-    finally:
-        _capi.set_launch_shape(3)
     assert torch.equal(outs[0][0].view(torch.int16), outs[1][0].view(torch.int16))
     assert torch.equal(outs[0][1].view(torch.int16), outs[1][1].view(torch.int16))

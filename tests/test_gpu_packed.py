@@ -85,6 +85,67 @@ def test_stable_norm_huge_values(dtype, lengths):
     assert torch.isfinite(out.float()).all()
 
 
+@pytest.mark.parametrize("lengths", [[1, 3, 60], [1, 1, 1]])  # row-streaming and decode kernels
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_stable_norm_group_max_at_2_pow_60(dtype, lengths):
+    """A 256-channel group whose conv outputs are all exactly +-2^60: 256 squares
+    of 2^60 sum to 2^128, which is inf in fp32, so the one-pass sum of squares
+    must not be used there (the rescaled form gives +-1). Rows just below
+    (2^60 (1 - 2^-8)) and just above (2^60 (1 + 2^-7)) the bound are checked
+    too. The filters pass the current input through unchanged (tap W-1 = 1,
+    the others 0), so y equals x exactly."""
+    D, W, G = 256, 4, 256
+    T = sum(lengths)
+    g = torch.Generator().manual_seed(60)
+    mags = torch.tensor([2.0 ** 60, 2.0 ** 60 * (1 - 2 ** -8), 2.0 ** 60 * (1 + 2 ** -7)], dtype=torch.float64)
+    sign = torch.where(torch.rand(T, D, generator=g) < 0.5, -1.0, 1.0).double()
+    x = (sign * mags[torch.arange(T) % 3][:, None]).to(dtype)
+    assert torch.equal(x.double().abs()[0], torch.full((D,), 2.0 ** 60, dtype=torch.float64))
+    w = torch.zeros(T, W, D // G, dtype=dtype)
+    w[:, W - 1] = 1.0
+    b = make_batch(lengths, [0, -1, 2], [0, 1, 0], 3, D, W, G, dtype, seed=61, gate_on=False)
+    b["x"], b["w"] = x, w
+    out = run_and_check(b, norm=True, dtype=dtype)
+    o = out.float().cpu()
+    assert torch.isfinite(o).all()
+    # every row's group is one magnitude, so the normalised row is +-1
+    torch.testing.assert_close(o, sign.float(), rtol=0, atol=1e-2)
+
+
+@pytest.mark.parametrize("layout", ["DS", "SD", "generic"])
+@pytest.mark.parametrize("D,W,G", [(4096, 4, 512), (2048, 7, 1024), (4096, 7, 4096), (1024, 3, 512), (2048, 2, 2048)])
+def test_wide_groups(layout, D, W, G):
+    """Groups wider than 256 channels (the reference's supports() accepts any
+    power of two dividing D, greta_vllm/triton_conv.py:119-121): one CTA per
+    group; mixed decodes and prefill chunks, padding slots, has_initial off,
+    requests shorter than W-1 and longer than a chunk."""
+    lengths = [1, 1, 1, 2, W - 1, 0, 17, 40]
+    slots = [3, -1, 7, 0, 11, 1, 5, 9]
+    init = [1, 1, 0, 1, 1, 0, 1, 0]
+    b = make_batch(lengths, slots, init, 12, D, W, G, torch.bfloat16, seed=D + W + G, layout=layout)
+    run_and_check(b)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16])
+@pytest.mark.parametrize("norm,gate_on", [(True, False), (False, True), (False, False)])
+def test_wide_groups_dtypes_norm_gate(dtype, norm, gate_on):
+    b = make_batch([1, 1, 5, 60], [0, 1, 2, 3], [1, 0, 1, 1], 4, 2048, 4, 512, dtype, seed=9, gate_on=gate_on)
+    run_and_check(b, norm=norm, dtype=dtype)
+
+
+@pytest.mark.parametrize("scale", [3e37, 2.0 ** 47, 2.0 ** 48, 2.0 ** 49])
+def test_wide_groups_stable_norm_large_values(scale):
+    """The overflow-safe norm of a 1024-channel group at and around its
+    one-pass bound (max|y| < 2^48) and near the fp32 limit: finite and within
+    tolerance of the oracle."""
+    b = make_batch([1, 3, 60], [0, -1, 2], [1, 1, 1], 3, 2048, 4, 1024, torch.float32, seed=19)
+    for k in ("x", "logical"):
+        b[k] = (b[k].float() * scale).float()
+    b["state"].copy_(b["logical"].to(DEV))
+    out = run_and_check(b, norm=True, dtype=torch.float32)
+    assert torch.isfinite(out.float()).all()
+
+
 def test_prefill_config_varlen_1024():
     """Varlen chunked prefill: 8 sequences with lengths ~U[32, 256] (sum <= 1024),
     C=4096, K=4, state [64, 4096, 3] ~ N(0,1) read from 8 distinct slots."""
@@ -210,7 +271,7 @@ def test_out_of_range_slot_is_skipped_and_reported():
 def test_unsupported_group_raises_reference_error():
     from greta_plugin_b200 import packed_dynamic_conv_triton, supports
 
-    assert supports(128, 2048) and not supports(3, 48) and not supports(512, 2048)
+    assert supports(128, 2048) and not supports(3, 48) and supports(512, 2048) and not supports(4096, 2048)
     b = make_batch([2], [0], [1], 1, 48, 4, 1, torch.bfloat16, seed=1)
     with pytest.raises(ValueError, match="power-of-two group size"):
         packed_dynamic_conv_triton(b["x"].to(DEV), torch.zeros(2, 4, 16, device=DEV, dtype=torch.bfloat16), None,

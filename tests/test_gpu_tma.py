@@ -18,18 +18,15 @@ def capi():
 
     _capi.device_errors(clear=True)
     yield _capi
-    _capi.set_tma(True)
     assert _capi.device_errors(clear=True) == 0
 
 
 def both(capi, fn):
-    capi.set_tma(True)
     a = fn()
     torch.cuda.synchronize()
-    capi.set_tma(False)
-    b = fn()
+    with capi.launch_options(register_path=True):
+        b = fn()
     torch.cuda.synchronize()
-    capi.set_tma(True)
     return a, b
 
 
@@ -117,11 +114,9 @@ def test_packed_prefill_with_state(capi, layout, W, G):
         return logical.transpose(1, 2).contiguous().to(DEV).transpose(1, 2)
 
     sa, sb = make_state(), make_state()
-    capi.set_tma(True)
     ya = packed_dynamic_conv_triton(x, w, gate, sa, starts, sl, ini, G)
-    capi.set_tma(False)
-    yb = packed_dynamic_conv_triton(x, w, gate, sb, starts, sl, ini, G)
-    capi.set_tma(True)
+    with capi.launch_options(register_path=True):
+        yb = packed_dynamic_conv_triton(x, w, gate, sb, starts, sl, ini, G)
     torch.cuda.synchronize()
     assert torch.equal(ya, yb)
     assert torch.equal(sa, sb)
@@ -164,14 +159,13 @@ def test_packed_prefill_range_boundaries(capi, D, W, G, seed):
     starts = torch.tensor([lead] + list(lead + np.cumsum(lens)), dtype=torch.int32, device=DEV)
     sl, ini = slots.to(DEV), init.to(DEV)
     outs = []
-    for tma in (True, False):
-        capi.set_tma(tma)
-        st = logical.to(DEV).clone()
-        y = torch.zeros(T, D, device=DEV, dtype=torch.bfloat16)
-        packed_dynamic_conv_triton(x, w, gate, st, starts, sl, ini, G, out=y)
+    for register_path in (False, True):
+        with capi.launch_options(register_path=register_path):
+            st = logical.to(DEV).clone()
+            y = torch.zeros(T, D, device=DEV, dtype=torch.bfloat16)
+            packed_dynamic_conv_triton(x, w, gate, st, starts, sl, ini, G, out=y)
         torch.cuda.synchronize()
         outs.append((y, st))
-    capi.set_tma(True)
     (ya, sa), (yb, sb) = outs
     assert torch.equal(ya[lead:], yb[lead:])
     assert torch.equal(sa, sb)
@@ -237,11 +231,9 @@ def test_packed_prefill_channel_split(capi, layout):
         return logical.transpose(1, 2).contiguous().to(DEV).transpose(1, 2)
 
     sa, sb = make_state(), make_state()
-    capi.set_tma(True)
     ya = packed_dynamic_conv_triton(x, w, gate, sa, starts, sl, ini, G)
-    capi.set_tma(False)
-    yb = packed_dynamic_conv_triton(x, w, gate, sb, starts, sl, ini, G)
-    capi.set_tma(True)
+    with capi.launch_options(register_path=True):
+        yb = packed_dynamic_conv_triton(x, w, gate, sb, starts, sl, ini, G)
     torch.cuda.synchronize()
     assert torch.equal(ya, yb)
     assert torch.equal(sa, sb)
@@ -322,3 +314,48 @@ def test_training_backward_single_sequence(capi):
     dxo, dwo, _ = oracle.bwd(to_np(x[0]), to_np(w), None, to_np(dout[0]), None, 1, 0)
     assert_close(a[0][0], dxo, torch.bfloat16)
     assert_close(a[1], dwo, torch.bfloat16)
+
+
+def test_pipeline_wait_runs_out_and_the_kernel_returns(capi):
+    """A bounded pipeline wait that runs out: with the test hook, consumer warp
+    0 of CTA 0 keeps the first stage it used, so CTA 0's producer waits for a
+    release that never comes. Its wait (2^14 polls) runs out, it records the
+    timeout bit and returns; CTA 0's consumers then wait for a stage that is
+    never filled and return the same way. Every bulk copy that was issued has
+    landed by then (the consumers waited for each), nothing faults, the call
+    returns, the error word reports the timeout, and the context runs normal
+    launches with correct results afterwards. 4096 tokens x 4096 channels:
+    each of the CTAs streams ~27 one-token stages through a ring of 5, so the
+    refill is reached."""
+    from greta_plugin_b200.dynamic_conv import dynconv_fwd
+
+    g = torch.Generator().manual_seed(77)
+    T, D, W = 4096, 4096, 4
+    x = rand(g, 1, T, D).to(DEV)
+    w = rand(g, T, W, D, scale=0.5).to(DEV)
+    capi.device_errors(clear=True)
+    with capi.launch_options(wait_limit_log2=14, test_withhold_release=True):
+        y_bad, _, _, _ = dynconv_fwd(x, w, None, None, 1)
+    torch.cuda.synchronize()
+    bits = capi.device_errors(clear=True)
+    assert bits & capi.ERR_BIT_TIMEOUT, f"expected the timeout bit, got {bits:#x}"
+    # the context is intact: a normal launch afterwards is correct and clean
+    y, _, _, _ = dynconv_fwd(x, w, None, None, 1)
+    torch.cuda.synchronize()
+    assert capi.device_errors(clear=True) == 0
+    yo, _ = oracle.fwd(to_np(x[0]), to_np(w), None, None, 1, 0)
+    assert_close(y[0], yo, torch.bfloat16)
+    # the other CTAs of the stopped launch finished their ranges: the last
+    # token rows (far from CTA 0's range) match
+    assert torch.equal(y_bad[0, -64:], y[0, -64:])
+    # the checked vLLM entry point turns the bit into an exception
+    from greta_plugin_b200.vllm_conv import packed_dynamic_conv_checked
+
+    starts = torch.tensor([0, T], dtype=torch.int32, device=DEV)
+    state = torch.zeros(1, D, W - 1, dtype=torch.bfloat16, device=DEV)
+    one = torch.ones(1, dtype=torch.int8, device=DEV)
+    slot = torch.zeros(1, dtype=torch.int32, device=DEV)
+    with capi.launch_options(wait_limit_log2=14, test_withhold_release=True):
+        with pytest.raises(capi.GretaKernelError, match="timed out"):
+            packed_dynamic_conv_checked(x[0], w, None, state, starts, slot, one, 1, norm=False)
+    assert capi.device_errors(clear=True) == 0

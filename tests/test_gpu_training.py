@@ -154,3 +154,31 @@ def test_bad_shapes_raise_reference_errors():
                               group_size=384)
     with pytest.raises(ValueError, match="weight must be"):
         dynamic_causal_conv1d(x[:1], torch.zeros(7, 4, 64, device=DEV))
+
+
+def test_config1_fp32_against_reference_checksums():
+    """Configuration 1 exactly: fp32, B=2 x T=256 packed with cu_seqlens
+    [0, 256, 512], C=512, K=4, x ~ N(0,1), w ~ N(0, 1/K), zero initial state,
+    forward only, seed 0. Checked on the GPU against the checksums and sampled
+    outputs of the reference's torch path (tests/golden/config1_stats.json,
+    made by tests/golden/make_golden.py) and elementwise against the oracle."""
+    import json
+
+    from conftest import GOLDEN
+    from greta_plugin_b200 import dynamic_causal_conv1d
+
+    s = json.loads((GOLDEN / "config1_stats.json").read_text())
+    g = torch.Generator().manual_seed(s["seed"])
+    x = torch.randn(*s["shape_x"], generator=g)
+    w = torch.randn(*s["shape_w"], generator=g) * s["w_scale"]
+    assert abs(float(x.double().sum()) - s["x_sum"]) < 1e-6 * max(1.0, abs(s["x_sum"]))
+    cu = torch.tensor(s["cu_seqlens"], dtype=torch.int32)
+    y = dynamic_causal_conv1d(x.to(DEV), w.to(DEV), None, cu.to(DEV), 1, False)
+    assert y.dtype == torch.float32 and y.shape == x.shape
+    yd = y.double().cpu()
+    assert abs(float(yd.sum()) - s["y_sum"]) < 1e-3
+    assert abs(float(yd.square().sum()) - s["y_sq"]) < 1e-6 * s["y_sq"]
+    assert abs(float(yd.abs().sum()) - s["y_abs"]) < 1e-6 * s["y_abs"]
+    np.testing.assert_allclose(y.reshape(-1)[s["sample_idx"]].cpu().numpy(), s["sample_val"], rtol=1e-5, atol=1e-6)
+    yo, _ = oracle.fwd(x[0].numpy(), w.numpy(), None, np.array(s["cu_seqlens"]), 1, 0)
+    assert_close(y[0], yo, torch.float32)
