@@ -26,7 +26,7 @@ _lib = None
 
 class Options(ctypes.Structure):
     """greta_dynconv_options: per-call launch choices of the `_ex` entry points."""
-    _fields_ = [("size", ctypes.c_int), ("register_path", ctypes.c_int), ("block_x", ctypes.c_int),
+    _fields_ = [("size", ctypes.c_int), ("kernel", ctypes.c_int), ("block_x", ctypes.c_int),
                 ("block_y", ctypes.c_int), ("tokens", ctypes.c_int), ("wait_limit_log2", ctypes.c_int),
                 ("test_withhold_release", ctypes.c_int)]
 
@@ -34,13 +34,18 @@ class Options(ctypes.Structure):
 _local = threading.local()
 
 
+KERNELS = {"auto": 0, "register": 1, "rows": 2}  # GRETA_KERNEL_*
+
+
 @contextlib.contextmanager
-def launch_options(register_path=False, block_x=0, block_y=0, tokens=0, wait_limit_log2=0,
-                   test_withhold_release=False):
+def launch_options(kernel="auto", block_x=0, block_y=0, tokens=0, wait_limit_log2=0, test_withhold_release=False):
     """Launch choices for the C-ABI calls this thread makes inside the block
-    (tests and tuning sweeps). They travel with each call as its options
-    argument; nothing is set in the library."""
-    o = Options(ctypes.sizeof(Options), int(bool(register_path)), block_x, block_y, tokens, wait_limit_log2,
+    (tests and tuning sweeps): the kernel family ("auto", "register", "rows"
+    for the row-streaming bulk-copy kernels), the register kernels' CTA
+    shape, the pipeline wait bound. They
+    travel with each call as its options argument; nothing is set in the
+    library."""
+    o = Options(ctypes.sizeof(Options), KERNELS[kernel], block_x, block_y, tokens, wait_limit_log2,
                 int(bool(test_withhold_release)))
     prev = getattr(_local, "opts", None)
     _local.opts = o

@@ -135,7 +135,7 @@ constexpr Shape kDefaultShape[kPaths] = {
 // Per-call launch choices (greta_dynconv_options); the library keeps no
 // process-wide settings.
 struct Opts {
-  bool reg = false;    // register-staged kernels only
+  int kernel = GRETA_KERNEL_AUTO;  // GRETA_KERNEL_*
   Shape shape{0, 0, 0};  // register-kernel CTA shape (tx == 0: built-in)
   int wait_log2 = 0;   // pipeline wait bound of the row-streaming kernels
   int withhold = 0;    // test hook of the row-streaming forward
@@ -146,7 +146,8 @@ int parse_opts(const greta_dynconv_options* o, Opts& out) {
   out = Opts{};
   if (o == nullptr) return GRETA_OK;
   if (o->size != (int)sizeof(greta_dynconv_options)) return GRETA_ERR_INVALID_ARG;
-  out.reg = o->register_path != 0;
+  if (o->kernel < GRETA_KERNEL_AUTO || o->kernel > GRETA_KERNEL_ROWS) return GRETA_ERR_INVALID_ARG;
+  out.kernel = o->kernel;
   if (o->block_x > 0 && o->block_y > 0 && o->tokens > 0) {
     if (o->block_x % 32 != 0 || o->block_x * o->block_y > 256) return GRETA_ERR_INVALID_ARG;
     out.shape = Shape{o->block_x, o->block_y, o->tokens};
@@ -198,7 +199,7 @@ int64_t slice_channels(int64_t D, int64_t max_c) {
 // sequences, and room for at least two token rows in flight. Returns -1 when
 // it does not.
 int try_rows_fwd(int dtype, RowsParams p, bool gate, int norm, void* stream, const Opts& o) {
-  if (o.reg) return -1;
+  if (o.kernel != GRETA_KERNEL_AUTO && o.kernel != GRETA_KERNEL_ROWS) return -1;
   p.wait_log2 = o.wait_log2;
   p.withhold = o.withhold;
   const int es = esize(dtype);
@@ -292,7 +293,7 @@ cudaError_t run_bwd_rows(int dtype, const BwdRowsParams& p, int norm, int gv, di
 // sequences, and room for two stages of token rows (x, filters, dout, gate,
 // saved pre-norm output). Returns -1 when it does not.
 int try_rows_bwd(int dtype, BwdRowsParams p, int norm, void* stream, const Opts& o) {
-  if (o.reg) return -1;
+  if (o.kernel != GRETA_KERNEL_AUTO && o.kernel != GRETA_KERNEL_ROWS) return -1;
   p.wait_log2 = o.wait_log2;
   const int es = esize(dtype);
   const int64_t D = p.D, W = p.W, G = p.G, DC = D / G;

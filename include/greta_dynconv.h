@@ -170,10 +170,15 @@ GRETA_API int greta_dynconv_packed_state(int dtype, const void* x, const void* w
  * results beyond floating-point summation order, except the test hooks,
  * which make a kernel stop early on purpose.
  */
+/* kernel families, for greta_dynconv_options.kernel */
+#define GRETA_KERNEL_AUTO 0     /* the library's choice per call */
+#define GRETA_KERNEL_REGISTER 1 /* register-staged kernels only */
+#define GRETA_KERNEL_ROWS 2     /* row-streaming (bulk-copy) kernels where the shape allows */
+
 typedef struct greta_dynconv_options {
   int size;          /* sizeof(greta_dynconv_options); other sizes are rejected */
-  int register_path; /* != 0: never use the row-streaming (bulk-copy) kernels; the
-                        register-staged kernels give the same bits */
+  int kernel;        /* GRETA_KERNEL_*: a family that does not apply to the call falls
+                        back to the register-staged kernels; all give the same bits */
   int block_x;       /* register-kernel CTA shape: threads along channels (multiple of 32), */
   int block_y;       /* token runs per CTA (block_x * block_y <= 256) and */
   int tokens;        /* tokens per run (raised to at least W-1); any <= 0 = built-in shape */

@@ -147,7 +147,8 @@ def test_launch_options_validate(lib):
     assert fwd(opts(block_x=128, block_y=4, tokens=8)) == C.ERR_INVALID_ARG  # more than 256 threads
     assert fwd(opts(wait_limit_log2=4)) == C.ERR_INVALID_ARG
     assert fwd(opts(wait_limit_log2=25)) == C.ERR_INVALID_ARG
-    assert fwd(opts(block_x=64, block_y=2, tokens=8, wait_limit_log2=12, register_path=1)) == C.OK
+    assert fwd(opts(kernel=3)) == C.ERR_INVALID_ARG
+    assert fwd(opts(block_x=64, block_y=2, tokens=8, wait_limit_log2=12, kernel=1)) == C.OK
     # no process-wide knobs remain in the ABI
     for gone in ("greta_dynconv_set_tma", "greta_dynconv_set_launch_shape"):
         assert not hasattr(lib, gone)

@@ -52,25 +52,48 @@ def _twin_modules(dtype, **cfg):
     return mg, (c_ref, m_ref), (c_k, m_k)
 
 
-@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
-def test_hf_training_autograd_through_reference_forward(dtype):
-    mg, (c_ref, m_ref), (c_k, m_k) = _twin_modules(dtype)
+def _train_step(m, h0, dy, install):
+    h = h0.clone().requires_grad_()
+    with rh.installed(hf=install):
+        y = m(h)
+        y.backward(dy)
+    return [y, h.grad] + [p.grad for _, p in m.named_parameters()]
+
+
+def test_hf_training_autograd_through_reference_forward_fp32():
+    """fp32: the B200 training kernels under the reference's autograd dispatch
+    equal its torch path to fp32 rounding (output, input grad, every weight grad)."""
+    mg, (c_ref, m_ref), (c_k, m_k) = _twin_modules(torch.float32)
     g = torch.Generator().manual_seed(3)
-    h0 = torch.randn(2, 37, c_ref.hidden_dim, generator=g).to(DEV, dtype)
-    dy = torch.randn(2, 37, c_ref.hidden_dim, generator=g).to(DEV, dtype)
-    outs = []
-    for m, install in ((m_ref, False), (m_k, True)):
-        h = h0.clone().requires_grad_()
-        with rh.installed(hf=install):
-            y = m(h)
-            y.backward(dy)
-        outs.append((y, h.grad, {n: p.grad for n, p in m.named_parameters()}))
-    (y_r, dh_r, pg_r), (y_k, dh_k, pg_k) = outs
-    close(y_k, y_r, dtype)
-    close(dh_k, dh_r, dtype)
-    lim = 2e-2 if dtype == torch.bfloat16 else 1e-4
-    for n in pg_r:
-        assert rel_err(pg_k[n], pg_r[n]) < lim, n
+    h0 = torch.randn(2, 37, c_ref.hidden_dim, generator=g).to(DEV)
+    dy = torch.randn(2, 37, c_ref.hidden_dim, generator=g).to(DEV)
+    ref = _train_step(m_ref, h0, dy, False)
+    got = _train_step(m_k, h0, dy, True)
+    close(got[0], ref[0], torch.float32)
+    close(got[1], ref[1], torch.float32)
+    for a, b in zip(got[2:], ref[2:]):
+        assert rel_err(a, b) < 1e-4
+
+
+def test_hf_training_autograd_through_reference_forward_bf16():
+    """bf16: a whole layer (three bf16 GEMMs around the conv) differs between
+    any two bf16 pipelines by a few bf16 ulps, so both -- the reference's own
+    torch path and the B200 kernels under its dispatch -- are measured against
+    the same layer in fp32 (same weights), and the B200 path must be as close
+    to it as the reference's path is (relative L2 error within 1.25x + 1e-3)."""
+    mg, (c_ref, m_ref), (c_k, m_k) = _twin_modules(torch.bfloat16)
+    rdc, mg, cg = rh.reference_modules()
+    c32, m32 = rh.make_hf_conv(mg, cg, torch.float32, DEV, 0, False)
+    m32.load_state_dict({k: v.float() for k, v in m_ref.state_dict().items()})
+    g = torch.Generator().manual_seed(3)
+    h0 = torch.randn(2, 37, c_ref.hidden_dim, generator=g).to(DEV, torch.bfloat16)
+    dy = torch.randn(2, 37, c_ref.hidden_dim, generator=g).to(DEV, torch.bfloat16)
+    exact = _train_step(m32, h0.float(), dy.float(), False)
+    ref = _train_step(m_ref, h0, dy, False)
+    got = _train_step(m_k, h0, dy, True)
+    for i, (a, b, e) in enumerate(zip(got, ref, exact)):
+        e_got, e_ref = rel_err(a, e), rel_err(b, e)
+        assert e_got <= 1.25 * e_ref + 1e-3, (i, e_got, e_ref)
 
 
 def test_hf_inference_without_cache_with_mask():

@@ -24,7 +24,7 @@ def capi():
 def both(capi, fn):
     a = fn()
     torch.cuda.synchronize()
-    with capi.launch_options(register_path=True):
+    with capi.launch_options(kernel="register"):
         b = fn()
     torch.cuda.synchronize()
     return a, b
@@ -115,7 +115,7 @@ def test_packed_prefill_with_state(capi, layout, W, G):
 
     sa, sb = make_state(), make_state()
     ya = packed_dynamic_conv_triton(x, w, gate, sa, starts, sl, ini, G)
-    with capi.launch_options(register_path=True):
+    with capi.launch_options(kernel="register"):
         yb = packed_dynamic_conv_triton(x, w, gate, sb, starts, sl, ini, G)
     torch.cuda.synchronize()
     assert torch.equal(ya, yb)
@@ -160,7 +160,7 @@ def test_packed_prefill_range_boundaries(capi, D, W, G, seed):
     sl, ini = slots.to(DEV), init.to(DEV)
     outs = []
     for register_path in (False, True):
-        with capi.launch_options(register_path=register_path):
+        with capi.launch_options(kernel="register" if register_path else "rows"):
             st = logical.to(DEV).clone()
             y = torch.zeros(T, D, device=DEV, dtype=torch.bfloat16)
             packed_dynamic_conv_triton(x, w, gate, st, starts, sl, ini, G, out=y)
@@ -232,7 +232,7 @@ def test_packed_prefill_channel_split(capi, layout):
 
     sa, sb = make_state(), make_state()
     ya = packed_dynamic_conv_triton(x, w, gate, sa, starts, sl, ini, G)
-    with capi.launch_options(register_path=True):
+    with capi.launch_options(kernel="register"):
         yb = packed_dynamic_conv_triton(x, w, gate, sb, starts, sl, ini, G)
     torch.cuda.synchronize()
     assert torch.equal(ya, yb)
@@ -355,7 +355,7 @@ def test_pipeline_wait_runs_out_and_the_kernel_returns(capi):
     state = torch.zeros(1, D, W - 1, dtype=torch.bfloat16, device=DEV)
     one = torch.ones(1, dtype=torch.int8, device=DEV)
     slot = torch.zeros(1, dtype=torch.int32, device=DEV)
-    with capi.launch_options(wait_limit_log2=14, test_withhold_release=True):
+    with capi.launch_options(kernel="rows", wait_limit_log2=14, test_withhold_release=True):
         with pytest.raises(capi.GretaKernelError, match="timed out"):
             packed_dynamic_conv_checked(x[0], w, None, state, starts, slot, one, 1, norm=False)
     assert capi.device_errors(clear=True) == 0
