@@ -214,9 +214,16 @@ def time_graph(torch, sets, launch, steps, warmup, dist, spread=None):
     torch.cuda.current_stream().wait_stream(stream)
     torch.cuda.synchronize()
     graph = torch.cuda.CUDAGraph()
+    # event nodes at the graph's first and last positions: they time the K
+    # steps on the device from the first launch to the end of the last, without
+    # the device-side start of the graph itself
+    first, last = (torch.cuda.Event(enable_timing=True, external=True),
+                   torch.cuda.Event(enable_timing=True, external=True))
     with torch.cuda.graph(graph, stream=stream):
+        first.record()
         for i in range(steps):
             launch(sets[i % len(sets)])
+        last.record()
     # warm replay (untimed), then the timed replay
     graph.replay()
     torch.cuda.synchronize()
@@ -231,10 +238,14 @@ def time_graph(torch, sets, launch, steps, warmup, dist, spread=None):
     end.synchronize()
     torch.cuda.synchronize()
     barrier(dist)
-    sec = start.elapsed_time(end) / 1e3
+    outer = start.elapsed_time(end) / 1e3
+    inner = first.elapsed_time(last) / 1e3
+    # the in-graph window when it is sane, else the held outer window
+    sec = inner if 0 < inner <= outer else outer
     del graph
     if spread is not None:
         spread.update(rank_spread(torch, dist, sec))
+        spread["outer_window"] = rank_spread(torch, dist, outer)["max"]
     return reduce_max(torch, dist, sec)
 
 
@@ -314,7 +325,7 @@ def run_prefill(torch, vc, dev, args, dist, rank, world, peak, traffic):
                 achieved_gbs=achieved, frac=achieved / peak, sets=len(sets), launches=steps + max(5, min(steps, 50)),
                 us_per_step_over_ranks={k: (v / steps * 1e6 if k != "ranks" else v) for k, v in spread.items()},
                 isolated=dict(us=iso * 1e6, frac=nbytes / iso / 1e9 / peak),
-                lengths=probe["lengths"], traffic=traffic.get("prefill"))
+                lengths=probe["lengths"], traffic=traffic.get("prefill"), channels=args.channels)
 
 
 def run_decode(torch, vc, dev, args, dist, rank, world, peak, traffic):
@@ -334,7 +345,33 @@ def run_decode(torch, vc, dev, args, dist, rank, world, peak, traffic):
                 launches=steps + max(5, min(steps, 50)),
                 us_per_step_over_ranks={k: (v / steps * 1e6 if k != "ranks" else v) for k, v in spread.items()},
                 isolated=dict(us=iso * 1e6, frac=nbytes / iso / 1e9 / peak),
-                traffic=traffic.get("decode"))
+                traffic=traffic.get("decode"), channels=args.channels)
+
+
+def run_channel_split(torch, vc, dev, args, dist, rank, world, peak):
+    """Multi-GPU mode of the north star: the channels of ONE batch split over
+    the ranks in contiguous, group-aligned shards (vLLM's column-parallel
+    layout, greta_plugin_b200.sharding.channel_shard); every rank runs the
+    kernels on its D/N channels of the same tokens, with no collective on the
+    data path. Aggregate tokens/s = the batch's tokens / the slowest rank's
+    step (strong scaling of the fixed batch); per-GPU fraction = a rank's
+    bytes / its step / the copy peak."""
+    import copy
+
+    from greta_plugin_b200.sharding import channel_shard
+
+    a = copy.copy(args)
+    a.shard = "channels"
+    a.channels = channel_shard(4096, 1, world, rank).channels
+    out = {"ranks": world, "channels_per_rank": a.channels, "collective": None}
+    for name, fn in (("prefill", run_prefill), ("decode", run_decode)):
+        r = fn(torch, vc, dev, a, dist, rank, world, peak, {})
+        out[name] = dict(tokens_per_step=r["tokens_per_step"], us_per_step=r["ms_per_step"] * 1e3,
+                         tokens_per_s=r["tokens_per_s"], per_gpu_frac=r["frac"], per_gpu_gbs=r["achieved_gbs"],
+                         isolated_us=r["isolated"]["us"], launches=r["launches"],
+                         us_per_step_over_ranks=r["us_per_step_over_ranks"])
+    out["launches"] = sum(out[k]["launches"] for k in ("prefill", "decode"))
+    return out
 
 
 def run_train(torch, dev, args, dist, rank, world, peak, traffic):
@@ -965,6 +1002,8 @@ def main():
             out["train"] = run_train(torch, dev, args, dist, rank, world, peak, traffic)
         if args.workload in ("greta", "all"):
             out["greta_layer"] = run_greta(torch, vc, dev, args, dist, rank, world, peak)
+        if world > 1 and args.shard == "requests" and args.workload in ("prefill", "all"):
+            out["channel_split"] = run_channel_split(torch, vc, dev, args, dist, rank, world, peak)
         e2e = run_e2e_prefill(torch, vc, dev, args, dist) if args.workload in ("prefill", "all") else None
     clk = clocks.summary()
     if args.workload == "all" and not args.no_reference_triton and world == 1:
