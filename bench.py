@@ -620,6 +620,60 @@ def run_reference_triton(torch, dev, args, dist, peak):
     return out
 
 
+def run_hf(torch, dev, args, dist, rank, peak):
+    """The HF plugin's two inference entry points (greta/dynamic_conv.py):
+    single-token decode keyed by batch row with the in-place state shift
+    (dynamic_causal_conv1d_decode, 256 rows) and the forward from an explicit
+    context (dynamic_causal_conv1d_inference, 8 rows of 112 query tokens), at
+    the headline shape (C=4096, K=4, G=1) and at Greta's layer shape (C=2048,
+    K=7, G=128, plain norm and gate). Graph-replayed like prefill/decode,
+    rotating over input sets of more than 2.5 x L2."""
+    from greta_plugin_b200 import dynamic_causal_conv1d_decode, dynamic_causal_conv1d_inference
+
+    out = {}
+    seed = 6000 + (rank if args.shard == "requests" else 0)
+    for shape, (D, W, G, norm) in (("headline", (args.channels, 4, 1, False)), ("greta_layer", (2048, 7, 128, True))):
+        gate_on = norm
+        F = D // G
+        # decode rows: x, w, (gate), y per row; the row's state read and written
+        B = 256
+        per_set = B * (2 * D * (2 + gate_on) + 2 * W * F + 4 * (W - 1) * D)
+
+        def dec_set(sd):
+            gd = torch.Generator(device=dev).manual_seed(sd)
+            return dict(x=torch.randn(B, D, device=dev, generator=gd).bfloat16(),
+                        w=(torch.randn(B, W, F, device=dev, generator=gd) * (1.0 / W) ** 0.5).bfloat16(),
+                        g=torch.randn(B, D, device=dev, generator=gd).bfloat16() if gate_on else None,
+                        s=torch.randn(B, D, W - 1, device=dev, generator=gd).bfloat16())
+
+        sets = [dec_set(seed + i) for i in range(n_sets(per_set))]
+        sec = time_graph(torch, sets, lambda b: dynamic_causal_conv1d_decode(b["x"], b["w"], b["s"], b["g"], G, norm),
+                         args.decode_steps, args.warmup, dist) / args.decode_steps
+        r = {"decode_rows": dict(rows=B, us=sec * 1e6, tokens_per_s=B / sec, bytes=per_set,
+                                 frac=per_set / sec / 1e9 / peak)}
+        del sets
+        # inference from context: context rows (W-1 history + Q), w, (gate), y
+        Bq, Q = 8, 112
+        per_set = Bq * (2 * (Q + W - 1) * D + Q * (2 * D * (1 + gate_on) + 2 * W * F))
+
+        def inf_set(sd):
+            gd = torch.Generator(device=dev).manual_seed(sd)
+            return dict(c=torch.randn(Bq, Q + W - 1, D, device=dev, generator=gd).bfloat16(),
+                        w=(torch.randn(Bq, Q, W, F, device=dev, generator=gd) * (1.0 / W) ** 0.5).bfloat16(),
+                        g=torch.randn(Bq, Q, D, device=dev, generator=gd).bfloat16() if gate_on else None)
+
+        sets = [inf_set(seed + 50 + i) for i in range(n_sets(per_set))]
+        sec = time_graph(torch, sets, lambda b: dynamic_causal_conv1d_inference(b["c"], b["w"], b["g"], G, norm),
+                         args.steps, args.warmup, dist) / args.steps
+        r["inference"] = dict(rows=Bq, query=Q, tokens=Bq * Q, us=sec * 1e6, tokens_per_s=Bq * Q / sec,
+                              bytes=per_set, frac=per_set / sec / 1e9 / peak)
+        del sets
+        r.update(channels=D, kernel_size=W, group_size=G, norm=norm, gate=gate_on)
+        out[shape] = r
+    out["launches"] = 2 * (args.decode_steps + args.steps)
+    return out
+
+
 def run_e2e_prefill(torch, vc, dev, args, dist):
     """Public API with host buffers: every step copies its inputs from pinned
     host memory (H2D), makes the call and copies the output back (D2H), all
@@ -848,7 +902,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--workload", choices=["prefill", "decode", "train", "greta", "all"], default="all")
+    ap.add_argument("--workload", choices=["prefill", "decode", "train", "greta", "hf", "all"], default="all")
     ap.add_argument("--shard", choices=["requests", "channels"], default="requests")
     ap.add_argument("--decode-steps", type=int, default=None)
     ap.add_argument("--train-steps", type=int, default=None)
@@ -1002,6 +1056,8 @@ def main():
             out["train"] = run_train(torch, dev, args, dist, rank, world, peak, traffic)
         if args.workload in ("greta", "all"):
             out["greta_layer"] = run_greta(torch, vc, dev, args, dist, rank, world, peak)
+        if args.workload in ("hf", "all"):
+            out["hf"] = run_hf(torch, dev, args, dist, rank, peak)
         if world > 1 and args.shard == "requests" and args.workload in ("prefill", "all"):
             out["channel_split"] = run_channel_split(torch, vc, dev, args, dist, rank, world, peak)
         e2e = run_e2e_prefill(torch, vc, dev, args, dist) if args.workload in ("prefill", "all") else None
@@ -1036,6 +1092,10 @@ def main():
             gp = out["greta_layer"]["prefill"]
             head = dict(tokens_per_s=gp["tokens_per_s"], ms_per_step=gp["us"] / 1e3,
                         achieved_gbs=gp["bytes"] / gp["us"] / 1e3, frac=gp["frac"])
+        if head is None and set(out) == {"hf"}:  # --workload hf: the headline-shape decode rows lead
+            hd = out["hf"]["headline"]["decode_rows"]
+            head = dict(tokens_per_s=hd["tokens_per_s"], ms_per_step=hd["us"] / 1e3,
+                        achieved_gbs=hd["bytes"] / hd["us"] / 1e3, frac=hd["frac"])
         if head is None:  # a single non-prefill workload was asked for
             key = next(iter(out))
             head = out[key]

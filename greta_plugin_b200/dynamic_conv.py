@@ -384,6 +384,76 @@ def dynamic_causal_conv1d_decode(
     return y
 
 
+@torch.compiler.disable(recursive=True)
+def dynamic_causal_conv1d_prefill_with_state(
+    x: torch.Tensor,
+    weight: torch.Tensor,
+    conv_state: torch.Tensor,
+    has_previous: bool,
+    gate: Optional[torch.Tensor] = None,
+    group_size: int = 1,
+    norm: bool = False,
+    norm_eps: float = 1e-6,
+) -> torch.Tensor:
+    """HF prefill chunk with a channel-first conv state, in one launch.
+
+    The reference does this in two steps: GretaDynamicCache.update_conv_inputs
+    (greta/modeling_greta.py:214-248) transposes the chunk to channel-first,
+    concatenates it with the cached state into [B, D, W-1+Q], keeps the last
+    W-1 columns as the new state and transposes the concatenation back into a
+    [B, Q+W-1, D] context, which dynamic_causal_conv1d_inference
+    (greta/dynamic_conv.py:643-687) then convolves. Here the kernel reads the
+    history of each batch row straight from conv_state (when has_previous;
+    zeros otherwise) and writes the row's last W-1 inputs back into it, bit
+    for bit: the same outputs (the same plain group RMS norm as the inference
+    kernel) and the same new state, with no context tensor.
+
+    x: [B, Q, D]; weight: [B, Q, W, D // group_size]; gate: [B, Q, D] or None;
+    conv_state: [B, D, W-1], contiguous, updated in place. Returns [B, Q, D].
+    """
+    for t in (x, weight, conv_state, gate):
+        if t is not None and not t.is_cuda:
+            raise ValueError("dynamic_causal_conv1d_prefill_with_state requires CUDA tensors")
+    if x.ndim != 3 or weight.ndim != 4:
+        raise ValueError(f"x must be [B, Q, D] and weight [B, Q, W, D // group_size], got "
+                         f"{tuple(x.shape)} and {tuple(weight.shape)}")
+    B, Q, D = x.shape
+    W = weight.shape[2]
+    _check_group(group_size)
+    if D % group_size != 0 or tuple(weight.shape) != (B, Q, W, D // group_size):
+        raise ValueError(f"weight must be [B, Q, W, D // group_size], got {tuple(weight.shape)}")
+    if W < 2:
+        raise ValueError("a conv state needs kernel_size >= 2")
+    if tuple(conv_state.shape) != (B, D, W - 1):
+        raise ValueError(f"conv_state must be {(B, D, W - 1)}, got {tuple(conv_state.shape)}")
+    if not conv_state.is_contiguous():
+        raise ValueError("conv_state must be contiguous because it is updated in-place")
+    if conv_state.dtype != x.dtype:
+        raise ValueError(f"conv_state dtype {conv_state.dtype} must match x dtype {x.dtype}")
+    if gate is not None and tuple(gate.shape) != (B, Q, D):
+        raise ValueError(f"gate shape {tuple(gate.shape)} must match x {tuple(x.shape)}")
+    y = torch.empty_like(x)
+    if B == 0 or Q == 0:
+        return y
+    # each batch row is one request of Q tokens whose cache slot is its state row
+    xk = x.contiguous().view(B * Q, D)
+    wk = _as(weight, x.dtype).contiguous().view(B * Q, W, D // group_size)
+    gk = None if gate is None else _as(gate, x.dtype).contiguous().view(B * Q, D)
+    dev = x.device
+    starts = torch.arange(0, B * Q + 1, Q, dtype=torch.int32, device=dev)
+    slots = torch.arange(B, dtype=torch.int32, device=dev)
+    init = torch.full((B,), 1 if has_previous else 0, dtype=torch.int8, device=dev)
+    s_slot, s_d, s_h = conv_state.stride()
+    with custom_device_ctx(dev.index):
+        st = _capi.lib().greta_dynconv_packed_state_ex(
+            _capi.dtype_code(x), _capi.ptr(xk), _capi.ptr(wk), _capi.ptr(gk), _capi.ptr(y), _capi.ptr(conv_state), B,
+            s_slot, s_d, s_h, _capi.ptr(starts), _capi.ptr(slots), _capi.ptr(init), B, B * Q, D, W, group_size,
+            _capi.NORM_PLAIN if norm else _capi.NORM_NONE, float(norm_eps), None, _capi.stream_of(x),
+            _capi.options())
+    _capi.check("greta_dynconv_packed_state", st)
+    return y
+
+
 def triton_dynamic_causal_conv1d_autograd_from_context(
     context: torch.Tensor,
     weights: torch.Tensor,
@@ -425,6 +495,7 @@ def triton_dynamic_causal_conv1d_autograd_from_context(
 
 
 __all__ = [
+    "dynamic_causal_conv1d_prefill_with_state",
     "triton_dynamic_causal_conv1d_autograd_from_context",
     "dynamic_causal_conv1d",
     "dynamic_causal_conv1d_decode",

@@ -19,7 +19,10 @@ installs the kernels. Point `vllm.general_plugins` at
 """
 from __future__ import annotations
 
+import functools
 import importlib
+
+import torch
 
 from . import dynamic_conv as _dc
 from . import vllm_conv as _vc
@@ -61,10 +64,76 @@ def _rebind(module_name: str, names: dict) -> list[str]:
     return done
 
 
-def install_hf() -> list[str]:
-    """Route the HF Transformers plugin's conv calls to the B200 kernels."""
+def _live_conv_state(module, mg, hidden_states, past_key_values, use_cache):
+    """The cache's conv state [B, D, W-1] for a prefill chunk that continues
+    a cached sequence, when the reference would run the Triton inference
+    kernel on it (GretaDynamicConv.forward, greta/modeling_greta.py:437-569:
+    a cache with a previous state, several query tokens, no gradient, CUDA,
+    use_triton_kernels); None otherwise."""
+    if not (use_cache and isinstance(past_key_values, mg.GretaDynamicCache)):
+        return None
+    if hidden_states.ndim != 3 or hidden_states.shape[1] < 2 or not hidden_states.is_cuda:
+        return None
+    if module.kernel_size < 2 or not module.config.use_triton_kernels:
+        return None
+    if torch.is_grad_enabled() and (hidden_states.requires_grad or any(p.requires_grad for p in module.parameters())):
+        return None
+    state = past_key_values.get_conv_state_for_decode(module.layer_idx)
+    if state is None or state.device != hidden_states.device or not state.is_contiguous():
+        return None
+    if state.dtype != module.in_proj.weight.dtype:
+        return None
+    return state
+
+
+def _fused_cached_prefill(original):
+    """GretaDynamicConv.forward in which a prefill chunk that continues a
+    cached sequence runs as ONE launch (dynamic_causal_conv1d_prefill_with_state:
+    history read from the channel-first cache state, the new last W-1 inputs
+    written back into it) instead of the cache's transpose / concatenate /
+    transpose context (greta/modeling_greta.py:229-247) followed by the
+    inference kernel. Every other case runs the reference's own forward."""
+    if getattr(original, "__greta_b200__", False):
+        return original
+
+    @functools.wraps(original)
+    def forward(self, hidden_states, past_key_values=None, use_cache=False, attention_mask=None):
+        import greta.modeling_greta as mg
+
+        state = _live_conv_state(self, mg, hidden_states, past_key_values, use_cache)
+        if state is None:
+            return original(self, hidden_states, past_key_values=past_key_values, use_cache=use_cache,
+                            attention_mask=attention_mask)
+        # the projections of greta/modeling_greta.py:444-459
+        batch_size, query_length, _ = hidden_states.shape
+        if attention_mask is not None:
+            if attention_mask.ndim != 2 or attention_mask.shape != (batch_size, query_length):
+                raise ValueError("Convolution attention_mask must match [batch, query_length]")
+            hidden_states = hidden_states.masked_fill(~attention_mask.bool().unsqueeze(-1), 0)
+        weights = self.kernel_proj(hidden_states).view(batch_size, query_length, self.kernel_size,
+                                                       self.num_filters)
+        conv_inputs = self.in_proj(hidden_states)
+        gate = self.gate_proj(hidden_states)
+        output = _dc.dynamic_causal_conv1d_prefill_with_state(conv_inputs, weights.to(conv_inputs.dtype), state, True,
+                                                              gate, self.group_size, self.norm, self.norm_eps)
+        return self.out_proj(output)
+
+    forward.__greta_b200__ = True
+    return forward
+
+
+def install_hf(fused_cache_prefill: bool = True) -> list[str]:
+    """Route the HF Transformers plugin's conv calls to the B200 kernels.
+
+    With fused_cache_prefill, GretaDynamicConv.forward is also wrapped so
+    that a prefill chunk continuing a cached sequence is one launch on the
+    cache's own state tensor (see _fused_cached_prefill)."""
     done = _rebind("greta.dynamic_conv", DYNAMIC_CONV_NAMES)
     done += _rebind("greta.modeling_greta", HF_GLOBALS)
+    if fused_cache_prefill:
+        mg = importlib.import_module("greta.modeling_greta")
+        mg.GretaDynamicConv.forward = _fused_cached_prefill(mg.GretaDynamicConv.forward)
+        done.append("greta.modeling_greta.GretaDynamicConv.forward")
     return done
 
 

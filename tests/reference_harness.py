@@ -84,6 +84,9 @@ def installed(hf=False, vllm=False):
         mod = importlib.import_module(mod_name)
         for n in names:
             saved.append((mod, n, getattr(mod, n)))
+    if hf:
+        conv_cls = importlib.import_module("greta.modeling_greta").GretaDynamicConv
+        saved.append((conv_cls, "forward", conv_cls.forward))
     try:
         if hf:
             integration.install_hf()

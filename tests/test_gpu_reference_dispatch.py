@@ -131,6 +131,79 @@ def test_hf_cached_prefill_then_decode_steps():
             assert torch.equal(s_k, s_r), f"conv state differs after tokens [{a}, {b})"
 
 
+def test_hf_chunked_prefill_with_cache_is_one_launch_on_the_cache_state():
+    """A prefill in two chunks (16 + 24 tokens) then decode steps, through the
+    reference's GretaDynamicConv.forward and cache: the second chunk continues
+    a cached sequence, which the installed forward runs as one launch on the
+    cache's channel-first state (no context tensor). Against the reference's
+    torch path and its own Triton kernels: outputs within tolerance, the cache
+    state bit-identical after every call."""
+    rdc, mg, cg = rh.reference_modules()
+    c_ref, m_ref = rh.make_hf_conv(mg, cg, torch.bfloat16, DEV, 0, False)
+    c_tri, m_tri = rh.make_hf_conv(mg, cg, torch.bfloat16, DEV, 0, True)
+    c_k, m_k = rh.make_hf_conv(mg, cg, torch.bfloat16, DEV, 0, True)
+    m_tri.load_state_dict(m_ref.state_dict())
+    m_k.load_state_dict(m_ref.state_dict())
+    li = rh.conv_layer_index(c_ref)
+    caches = [rh.make_cache(mg, c) for c in (c_ref, c_tri, c_k)]
+    g = torch.Generator().manual_seed(15)
+    h = torch.randn(3, 43, c_ref.hidden_dim, generator=g).to(DEV, torch.bfloat16)
+    spans = [(0, 16), (16, 40), (40, 41), (41, 42), (42, 43)]
+    from greta_plugin_b200 import dynamic_conv as bdc
+
+    calls = []
+    orig = bdc.dynamic_causal_conv1d_prefill_with_state
+
+    def counting(*a, **k):
+        calls.append(1)
+        return orig(*a, **k)
+
+    bdc.dynamic_causal_conv1d_prefill_with_state = counting
+    try:
+        with torch.no_grad():
+            for a, b in spans:
+                y_r = m_ref(h[:, a:b], past_key_values=caches[0], use_cache=True)
+                y_t = m_tri(h[:, a:b], past_key_values=caches[1], use_cache=True)
+                with rh.installed(hf=True):
+                    y_k = m_k(h[:, a:b], past_key_values=caches[2], use_cache=True)
+                close(y_k, y_r, torch.bfloat16)
+                close(y_k, y_t, torch.bfloat16)
+                s_r, s_t, s_k = (c.layers[li].conv_states[0] for c in caches)
+                assert torch.equal(s_k, s_r) and torch.equal(s_k, s_t), f"state differs after [{a}, {b})"
+    finally:
+        bdc.dynamic_causal_conv1d_prefill_with_state = orig
+    assert len(calls) == 1  # the second prefill chunk
+
+
+@pytest.mark.parametrize("has_previous", [True, False])
+@pytest.mark.parametrize("Q", [1, 2, 9])
+def test_prefill_with_state_against_reference_cache_and_kernel(has_previous, Q):
+    """dynamic_causal_conv1d_prefill_with_state against the reference's two
+    steps: the cache's update_conv_inputs (context and new state) and its
+    Triton inference kernel on that context; chunks shorter than W-1 included."""
+    rdc, mg, cg = rh.reference_modules()
+    from greta_plugin_b200 import dynamic_causal_conv1d_prefill_with_state
+
+    cfg = rh.greta_config(cg)
+    li = rh.conv_layer_index(cfg)
+    B, D, W, G = 3, cfg.hidden_dim, cfg.kernel_size, cfg.conv_group_size
+    g = torch.Generator().manual_seed(16 + Q)
+    x = torch.randn(B, Q, D, generator=g).bfloat16().to(DEV)
+    wq = (torch.randn(B, Q, W, D // G, generator=g) * (1.0 / W) ** 0.5).bfloat16().to(DEV)
+    gq = torch.randn(B, Q, D, generator=g).bfloat16().to(DEV)
+    cache = rh.make_cache(mg, cfg)
+    if has_previous:  # a cached sequence: the state of an earlier chunk
+        cache.update_conv_inputs(torch.randn(B, 8, D, generator=g).bfloat16().to(DEV), li, W)
+    state = cache.layers[li].conv_states[0].clone() if has_previous else torch.zeros(B, D, W - 1, dtype=x.dtype,
+                                                                                    device=DEV)
+    ctx = cache.update_conv_inputs(x, li, W)
+    y_ref = rdc.dynamic_causal_conv1d_inference(ctx, wq, gq, G, True, 1e-6)
+    y = dynamic_causal_conv1d_prefill_with_state(x, wq, state, has_previous, gq, G, True, 1e-6)
+    close(y, y_ref, torch.bfloat16)
+    if Q >= W - 1 or has_previous:
+        assert torch.equal(state, cache.layers[li].conv_states[0]), "the new conv state must be bit-exact"
+
+
 # ---------------------------------------------------------------------------
 # vLLM
 # ---------------------------------------------------------------------------

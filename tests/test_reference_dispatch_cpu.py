@@ -47,8 +47,9 @@ def test_install_rebinds_and_restores_reference_names():
     from greta_plugin_b200 import vllm_conv as bvc
 
     before = (mg._TRITON_DYNAMIC_CAUSAL_CONV1D_DECODE, vm.packed_dynamic_conv_triton, vm.triton_supports,
-              rdc.dynconv_fwd)
+              rdc.dynconv_fwd, mg.GretaDynamicConv.forward)
     with rh.installed(hf=True, vllm=True):
+        assert getattr(mg.GretaDynamicConv.forward, "__greta_b200__", False)
         assert mg._TRITON_DYNAMIC_CAUSAL_CONV1D is bdc.dynamic_causal_conv1d
         assert mg._TRITON_DYNAMIC_CAUSAL_CONV1D_DECODE is bdc.dynamic_causal_conv1d_decode
         assert mg._TRITON_DYNAMIC_CAUSAL_CONV1D_INFERENCE is bdc.dynamic_causal_conv1d_inference
@@ -59,7 +60,7 @@ def test_install_rebinds_and_restores_reference_names():
         assert vtc.packed_dynamic_conv_triton is bvc.packed_dynamic_conv_triton
         assert rdc.dynconv_fwd is bdc.dynconv_fwd
     after = (mg._TRITON_DYNAMIC_CAUSAL_CONV1D_DECODE, vm.packed_dynamic_conv_triton, vm.triton_supports,
-             rdc.dynconv_fwd)
+             rdc.dynconv_fwd, mg.GretaDynamicConv.forward)
     assert all(a is b for a, b in zip(before, after))
 
 
@@ -107,3 +108,22 @@ def test_harness_skips_cleanly_without_reference(monkeypatch, tmp_path):
     assert not conftest.reference_available()
     with pytest.raises(pytest.skip.Exception):
         conftest.import_reference_path()
+
+
+def test_wrapped_forward_falls_back_to_the_reference_on_cpu():
+    """Off the GPU (and without a live cache state) the wrapped forward is the
+    reference's own: same output as the unwrapped module, cache state included."""
+    rdc, mg, cg = rh.reference_modules()
+    cfg, mod = rh.make_hf_conv(mg, cg, torch.float32, "cpu", 0, False, hidden_dim=256)
+    g = torch.Generator().manual_seed(7)
+    h = torch.randn(2, 10, 256, generator=g)
+    c1, c2 = rh.make_cache(mg, cfg), rh.make_cache(mg, cfg)
+    with torch.no_grad():
+        ref = [mod(h[:, :6], past_key_values=c1, use_cache=True), mod(h[:, 6:], past_key_values=c1, use_cache=True)]
+        with rh.installed(hf=True):
+            got = [mod(h[:, :6], past_key_values=c2, use_cache=True),
+                   mod(h[:, 6:], past_key_values=c2, use_cache=True)]
+    for a, b in zip(got, ref):
+        torch.testing.assert_close(a, b, rtol=0, atol=0)
+    li = rh.conv_layer_index(cfg)
+    assert torch.equal(c1.layers[li].conv_states[0], c2.layers[li].conv_states[0])
