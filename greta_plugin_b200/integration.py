@@ -132,6 +132,9 @@ def install_hf(fused_cache_prefill: bool = True) -> list[str]:
     done += _rebind("greta.modeling_greta", HF_GLOBALS)
     if fused_cache_prefill:
         mg = importlib.import_module("greta.modeling_greta")
+        if not hasattr(mg, "GretaDynamicConv"):
+            raise AttributeError("greta.modeling_greta has no attribute 'GretaDynamicConv'; "
+                                 "unexpected reference version")
         mg.GretaDynamicConv.forward = _fused_cached_prefill(mg.GretaDynamicConv.forward)
         done.append("greta.modeling_greta.GretaDynamicConv.forward")
     return done

@@ -102,6 +102,11 @@ def _fake_reference(monkeypatch):
             setattr(m, a, sentinel)
         mods[name] = m
         monkeypatch.setitem(sys.modules, name, m)
+    class GretaDynamicConv:
+        def forward(self, hidden_states, past_key_values=None, use_cache=False, attention_mask=None):
+            return "reference forward"
+
+    mods["greta.modeling_greta"].GretaDynamicConv = GretaDynamicConv
     calls = []
     mods["greta_vllm"].register = lambda: calls.append("reference register")
     return mods, sentinel, calls
@@ -119,6 +124,14 @@ def test_install_rebinds_reference_names(monkeypatch):
                 assert v is not sentinel, f"{name}.{attr} was not rebound"
     assert mods["greta_vllm.model"].triton_supports(128, 4096)
     assert mods["greta.modeling_greta"]._TRITON_DYNAMIC_CAUSAL_CONV1D is dynamic_causal_conv1d
+    # the cached-prefill wrapper is installed once and keeps the reference
+    # forward for everything it does not take (here: no cache)
+    cls = mods["greta.modeling_greta"].GretaDynamicConv
+    assert getattr(cls.forward, "__greta_b200__", False)
+    wrapped = cls.forward
+    integration.install_hf()
+    assert cls.forward is wrapped
+    assert cls().forward(torch.zeros(1, 2, 4)) == "reference forward"
 
 
 def test_install_refuses_unknown_reference_version(monkeypatch):
