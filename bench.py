@@ -136,9 +136,13 @@ def prefill_lengths(gen, torch):
             return lengths
 
 
-def make_prefill(torch, dev, seed, D=4096, W=4, G=1, n_slots=64):
+def make_prefill(torch, dev, seed, D=4096, W=4, G=1, n_slots=64, lengths=None):
+    """One prefill batch. `lengths` (default: drawn from the seed) fixes the
+    request lengths, so that rotating input sets hold the same batch shape
+    with different values."""
     g = torch.Generator().manual_seed(seed)
-    lengths = prefill_lengths(g, torch)
+    drawn = prefill_lengths(g, torch)
+    lengths = list(lengths) if lengths is not None else drawn
     T = sum(lengths)
     slots = torch.randperm(n_slots, generator=g)[:8].to(torch.int32)
     gd = torch.Generator(device=dev).manual_seed(seed)
@@ -313,7 +317,8 @@ def run_prefill(torch, vc, dev, args, dist, rank, world, peak, traffic):
     probe = make_prefill(torch, dev, base_seed, D=args.channels)
     nbytes = prefill_bytes(probe)
     for i in range(n_sets(nbytes + probe["state"].numel() * 2)):
-        sets.append(probe if i == 0 else make_prefill(torch, dev, base_seed + 97 * i, D=args.channels))
+        sets.append(probe if i == 0 else make_prefill(torch, dev, base_seed + 97 * i, D=args.channels,
+                                                      lengths=probe["lengths"]))
     steps = args.steps
     spread = {}
     sec = time_graph(torch, sets, lambda b: packed_call(vc, b), steps, args.warmup, dist, spread)
@@ -456,8 +461,8 @@ def run_greta(torch, vc, dev, args, dist, rank, world, peak):
     # prefill: x, gate, y per token, filters, old + new slot taps per request
     probe = add_gate(make_prefill(torch, dev, seed, D=D, W=W, G=G), seed)
     nb = probe["T"] * (6 * D + wb) + probe["N"] * 4 * (W - 1) * D
-    sets = [probe] + [add_gate(make_prefill(torch, dev, seed + 97 * i, D=D, W=W, G=G), seed + 97 * i)
-                      for i in range(1, n_sets(nb + probe["state"].numel() * 2))]
+    sets = [probe] + [add_gate(make_prefill(torch, dev, seed + 97 * i, D=D, W=W, G=G, lengths=probe["lengths"]),
+                               seed + 97 * i) for i in range(1, n_sets(nb + probe["state"].numel() * 2))]
     sec = time_graph(torch, sets, call, args.steps, args.warmup, dist) / args.steps
     out["prefill"] = dict(tokens=probe["T"], us=sec * 1e6, tokens_per_s=probe["T"] / sec, bytes=nb,
                           frac=nb / sec / 1e9 / peak)
@@ -544,7 +549,8 @@ def run_reference_triton(torch, dev, args, dist, peak):
     seed = 1000 + (int(os.environ.get("RANK", "0")) if args.shard == "requests" else 0)
     probe = make_prefill(torch, dev, seed, D=D)
     nb = prefill_bytes(probe)
-    sets = [probe] + [make_prefill(torch, dev, seed + 97 * i, D=D) for i in range(1, n_sets(nb + probe["state"].numel() * 2))]
+    sets = [probe] + [make_prefill(torch, dev, seed + 97 * i, D=D, lengths=probe["lengths"])
+                      for i in range(1, n_sets(nb + probe["state"].numel() * 2))]
     sec = time_graph(torch, sets, packed, args.steps, args.warmup, dist) / args.steps
     out["prefill"] = dict(tokens=probe["T"], us=sec * 1e6, tokens_per_s=probe["T"] / sec, frac=nb / sec / 1e9 / peak)
     del sets, probe
@@ -565,7 +571,9 @@ def run_reference_triton(torch, dev, args, dist, peak):
     gl = {}
     for name, mk, steps in (("prefill", make_prefill, args.steps), ("decode", make_decode, args.decode_steps)):
         probe = with_gate(mk(torch, dev, 5000, D=Dg, W=Wg, G=Gg), 5000)
-        sets = [probe] + [with_gate(mk(torch, dev, 5000 + 31 * i, D=Dg, W=Wg, G=Gg), 5000 + 31 * i) for i in range(1, 6)]
+        same = {"lengths": probe["lengths"]} if name == "prefill" else {}
+        sets = [probe] + [with_gate(mk(torch, dev, 5000 + 31 * i, D=Dg, W=Wg, G=Gg, **same), 5000 + 31 * i)
+                          for i in range(1, 6)]
         sec = time_graph(torch, sets, lambda b: packed(b, Gg, True), steps, args.warmup, dist) / steps
         gl[name] = dict(tokens=probe["T"], us=sec * 1e6, tokens_per_s=probe["T"] / sec)
         del sets, probe

@@ -28,7 +28,8 @@ class Options(ctypes.Structure):
     """greta_dynconv_options: per-call launch choices of the `_ex` entry points."""
     _fields_ = [("size", ctypes.c_int), ("kernel", ctypes.c_int), ("block_x", ctypes.c_int),
                 ("block_y", ctypes.c_int), ("tokens", ctypes.c_int), ("wait_limit_log2", ctypes.c_int),
-                ("test_withhold_release", ctypes.c_int)]
+                ("test_withhold_release", ctypes.c_int), ("rows_channels", ctypes.c_int),
+                ("rows_ranges", ctypes.c_int), ("rows_smem_kb", ctypes.c_int)]
 
 
 _local = threading.local()
@@ -38,15 +39,17 @@ KERNELS = {"auto": 0, "register": 1, "rows": 2}  # GRETA_KERNEL_*
 
 
 @contextlib.contextmanager
-def launch_options(kernel="auto", block_x=0, block_y=0, tokens=0, wait_limit_log2=0, test_withhold_release=False):
+def launch_options(kernel="auto", block_x=0, block_y=0, tokens=0, wait_limit_log2=0, test_withhold_release=False,
+                   rows_channels=0, rows_ranges=0, rows_smem_kb=0):
     """Launch choices for the C-ABI calls this thread makes inside the block
     (tests and tuning sweeps): the kernel family ("auto", "register", "rows"
     for the row-streaming bulk-copy kernels), the register kernels' CTA
-    shape, the pipeline wait bound. They
+    shape, the pipeline wait bound, the row-streaming kernels' channel slice,
+    token ranges and stage-ring budget. They
     travel with each call as its options argument; nothing is set in the
     library."""
     o = Options(ctypes.sizeof(Options), KERNELS[kernel], block_x, block_y, tokens, wait_limit_log2,
-                int(bool(test_withhold_release)))
+                int(bool(test_withhold_release)), rows_channels, rows_ranges, rows_smem_kb)
     prev = getattr(_local, "opts", None)
     _local.opts = o
     try:

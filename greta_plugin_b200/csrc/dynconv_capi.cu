@@ -139,6 +139,9 @@ struct Opts {
   Shape shape{0, 0, 0};  // register-kernel CTA shape (tx == 0: built-in)
   int wait_log2 = 0;   // pipeline wait bound of the row-streaming kernels
   int withhold = 0;    // test hook of the row-streaming forward
+  int rows_channels = 0;  // row-streaming kernels: channel-slice cap (0: built-in)
+  int rows_ranges = 0;    // row-streaming kernels: token ranges (0: SMs / slices)
+  int rows_smem = 200 * 1024;  // row-streaming kernels: stage-ring budget (bytes)
 };
 
 // GRETA_OK and the parsed options, or GRETA_ERR_INVALID_ARG for a bad struct.
@@ -155,6 +158,12 @@ int parse_opts(const greta_dynconv_options* o, Opts& out) {
   if (o->wait_limit_log2 != 0 && (o->wait_limit_log2 < 8 || o->wait_limit_log2 > 24)) return GRETA_ERR_INVALID_ARG;
   out.wait_log2 = o->wait_limit_log2;
   out.withhold = o->test_withhold_release != 0 ? 1 : 0;
+  if (o->rows_channels < 0 || (o->rows_channels > 0 && o->rows_channels < 256)) return GRETA_ERR_INVALID_ARG;
+  if (o->rows_ranges < 0 || o->rows_ranges > (1 << 20)) return GRETA_ERR_INVALID_ARG;
+  if (o->rows_smem_kb != 0 && (o->rows_smem_kb < 32 || o->rows_smem_kb > 200)) return GRETA_ERR_INVALID_ARG;
+  out.rows_channels = o->rows_channels;
+  out.rows_ranges = o->rows_ranges;
+  if (o->rows_smem_kb != 0) out.rows_smem = o->rows_smem_kb * 1024;
   return GRETA_OK;
 }
 
@@ -212,7 +221,9 @@ int try_rows_fwd(int dtype, RowsParams p, bool gate, int norm, void* stream, con
     if (!aligned(q, 16)) return -1;
   // the W template launch_fwd_rows picks: 4, 7, -8 or -kMaxWGeneric
   const int wt = W == 4 ? 4 : (W == 7 ? 7 : (W <= 8 ? -8 : -kMaxWGeneric));
-  const int64_t dcta = slice_channels(D, fwd_rows_max_channels(wt));
+  int64_t cmax = fwd_rows_max_channels(wt);
+  if (o.rows_channels > 0 && o.rows_channels < cmax) cmax = o.rows_channels;
+  const int64_t dcta = slice_channels(D, cmax);
   if (dcta == 0) return -1;
   const int64_t nsplit = D / dcta;
   if ((W * DC * es) % 16 != 0) return -1;
@@ -224,7 +235,7 @@ int try_rows_fwd(int dtype, RowsParams p, bool gate, int norm, void* stream, con
   const size_t off_meta = packed ? (size_t)(p.nseq + 1) * 8 : 0;
   const size_t meta = packed && p.state != nullptr ? (size_t)p.nseq * 5 : 0;
   const size_t off_stage = packed ? a128(off_meta + meta) : 0;
-  const size_t budget = 200 * 1024;
+  const size_t budget = (size_t)o.rows_smem;
   if (off_stage >= budget) return -1;
   const int64_t per_token = rowx + roww + (gate ? rowx : 0);
   const int64_t inflight = (int64_t)(budget - off_stage) / per_token;
@@ -259,7 +270,7 @@ int try_rows_fwd(int dtype, RowsParams p, bool gate, int norm, void* stream, con
   p.wsplit = wsplit ? 1 : 0;
   p.log2g = 0;
   while ((1 << p.log2g) < G) ++p.log2g;
-  long long ranges = num_sms() / nsplit;
+  long long ranges = o.rows_ranges > 0 ? o.rows_ranges : num_sms() / nsplit;
   if (ranges < 1) ranges = 1;
   if (p.U < ranges) ranges = p.U;
   if (ranges <= 0) return GRETA_OK;
@@ -303,7 +314,9 @@ int try_rows_bwd(int dtype, BwdRowsParams p, int norm, void* stream, const Opts&
     if (!aligned(q, 16)) return -1;
   // the W template launch_bwd_rows picks: 4, 7 or -kMaxWBwdRows
   const int wt = W == 4 ? 4 : (W == 7 ? 7 : -kMaxWBwdRows);
-  const int64_t dcta = slice_channels(D, bwd_rows_max_channels(wt, group_vec(kVec, G)));
+  int64_t cmax = bwd_rows_max_channels(wt, group_vec(kVec, G));
+  if (o.rows_channels > 0 && o.rows_channels < cmax) cmax = o.rows_channels;
+  const int64_t dcta = slice_channels(D, cmax);
   if (dcta == 0) return -1;
   const int64_t nsplit = D / dcta;
   if ((W * DC * es) % 16 != 0) return -1;
@@ -314,7 +327,7 @@ int try_rows_bwd(int dtype, BwdRowsParams p, int norm, void* stream, const Opts&
   const bool gate = p.g != nullptr, has_yr = norm != GRETA_NORM_NONE;
   const bool packed = p.mode == kModePacked;
   const size_t off_stage = packed ? a128((size_t)(p.nseq + 1) * 8) : 0;
-  const size_t budget = 200 * 1024;
+  const size_t budget = (size_t)o.rows_smem;
   if (off_stage >= budget) return -1;
   const int64_t per_token = 2 * rowx + roww + (gate ? rowx : 0) + (has_yr ? rowx : 0);
   const int64_t inflight = (int64_t)(budget - off_stage) / per_token;
@@ -350,7 +363,7 @@ int try_rows_bwd(int dtype, BwdRowsParams p, int norm, void* stream, const Opts&
   p.dcta = (int)dcta;
   p.nsplit = (int)nsplit;
   p.wsplit = wsplit ? 1 : 0;
-  long long ranges = num_sms() / nsplit;
+  long long ranges = o.rows_ranges > 0 ? o.rows_ranges : num_sms() / nsplit;
   if (ranges < 1) ranges = 1;
   if (p.T < ranges) ranges = p.T;
   if (ranges <= 0) return GRETA_OK;

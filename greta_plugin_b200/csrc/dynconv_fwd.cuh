@@ -273,10 +273,13 @@ __global__ void __launch_bounds__(256) dynconv_fwd_kernel(const FwdParams p) {
     load_old_state<T, NV, WT, MAXH>(p, ci, d0, active, H, hw);
     if (write_back && !wb_window) store_state_taps<T, NV, WT, MAXH>(p, ci, d0, H, tail);
   } else {
+    // only a thread with tokens loads history: the run of a thread past the
+    // end of its chunk (rs >= re) may lie past the end of the request, and
+    // for the last request past the end of x
 #pragma unroll
     for (int i = 0; i < MAXH; ++i) {
       zero(hw[i]);
-      if (i < H && active) {
+      if (i < H && active && rs < re) {
         const long long q = rs - 1 - i;
         if (q >= 0 || ci.hist == kHistX) hw[i] = ld<T, NV>(xg + (ci.x_base + q) * D + d0);
       }

@@ -188,6 +188,12 @@ typedef struct greta_dynconv_options {
                                 row-streaming forward keep its first stage, so that the
                                 producer's bounded wait runs out (device error bit 1, see
                                 greta_dynconv_device_errors); the launch still returns */
+  int rows_channels; /* row-streaming kernels: at most this many channels per CTA (the
+                        widest multiple of 256 dividing D that fits); 0 = built-in */
+  int rows_ranges;   /* row-streaming kernels: token ranges (CTAs = ranges x channel
+                        slices); 0 = SMs / slices */
+  int rows_smem_kb;  /* row-streaming kernels: shared-memory budget of the stage ring in
+                        KiB (32..200); 0 = 200 */
 } greta_dynconv_options;
 
 GRETA_API int greta_dynconv_fwd_ex(int dtype, const void* x, const void* w, const void* gate, void* y,
