@@ -206,6 +206,9 @@ def hold_stream(torch, stream, us=200):
         torch.cuda._sleep(int(us * 2.0e3))  # cycles at up to 2 GHz
 
 
+LEAD = 2  # untimed launches ahead of the timed ones in a replayed graph
+
+
 def time_graph(torch, sets, launch, steps, warmup, dist, spread=None):
     """Replay `steps` launches (rotating over `sets`) from one CUDA graph.
     Returns seconds for the K timed steps (max over ranks); `spread`, when
@@ -218,12 +221,17 @@ def time_graph(torch, sets, launch, steps, warmup, dist, spread=None):
     torch.cuda.current_stream().wait_stream(stream)
     torch.cuda.synchronize()
     graph = torch.cuda.CUDAGraph()
-    # event nodes at the graph's first and last positions: they time the K
-    # steps on the device from the first launch to the end of the last, without
-    # the device-side start of the graph itself
+    # Event nodes around the K timed launches time them on the device. LEAD
+    # untimed launches come first in the same graph, so that the first timed
+    # step, like every later one, follows a step of the same stream (a kernel
+    # launched with programmatic dependent launch overlaps its start-up with
+    # the end of the kernel ahead of it): the window holds K steps in steady
+    # state, not the start-up of the graph's first kernel.
     first, last = (torch.cuda.Event(enable_timing=True, external=True),
                    torch.cuda.Event(enable_timing=True, external=True))
     with torch.cuda.graph(graph, stream=stream):
+        for i in range(LEAD):
+            launch(sets[(steps + i) % len(sets)])
         first.record()
         for i in range(steps):
             launch(sets[i % len(sets)])
@@ -242,10 +250,10 @@ def time_graph(torch, sets, launch, steps, warmup, dist, spread=None):
     end.synchronize()
     torch.cuda.synchronize()
     barrier(dist)
-    outer = start.elapsed_time(end) / 1e3
+    outer = start.elapsed_time(end) / 1e3 * steps / (steps + LEAD)  # scaled to K steps
     inner = first.elapsed_time(last) / 1e3
     # the in-graph window when it is sane, else the held outer window
-    sec = inner if 0 < inner <= outer else outer
+    sec = inner if 0 < inner <= outer * (steps + LEAD) / steps else outer
     del graph
     if spread is not None:
         spread.update(rank_spread(torch, dist, sec))
@@ -522,6 +530,62 @@ def run_greta(torch, vc, dev, args, dist, rank, world, peak):
     out["train"] = dict(tokens=T, fwd_us=f_s * 1e6, bwd_us=b_s * 1e6, fwd_frac=fb / f_s / 1e9 / peak,
                         bwd_frac=bb / b_s / 1e9 / peak, fwd_bytes=fb, bwd_bytes=bb)
     out["launches"] = args.steps + args.decode_steps + 2 * steps
+    return out
+
+
+def run_tp_layer(torch, dev, args, dist, rank, world):
+    """The whole GretaConv layer of a vLLM step (greta_vllm/model.py:115-124) at
+    Greta's defaults (hidden 2048, W = 7, G = 128, norm + gate), split over the
+    N ranks as tensor parallelism (greta_plugin_b200.tp): column-parallel
+    in/gate/kernel projections, the B200 conv on D/N channels and the rank's
+    state slice, row-parallel out_proj and an NCCL all-reduce of the layer
+    output. Two projection forms: three GEMMs (the reference's) and one GEMM
+    over the concatenated weights, whose output the conv reads in place.
+    Decode (256 requests) and prefill (the headline's 8 request lengths);
+    plain launches between events, max over ranks."""
+    from greta_plugin_b200.tp import TPGretaConv, shard_layer_weights
+
+    hidden, D, W, G = 2048, 2048, 7, 128
+    Fn = D // G
+    gw = torch.Generator(device=dev).manual_seed(777)  # the same layer on every rank
+    sc = hidden ** -0.5
+    full = [torch.randn(D, hidden, device=dev, generator=gw) * sc for _ in range(2)]
+    kw = torch.randn(W * Fn, hidden, device=dev, generator=gw) * sc
+    kb = torch.randn(W * Fn, device=dev, generator=gw) * 0.1
+    ow = torch.randn(hidden, D, device=dev, generator=gw) * D ** -0.5
+    wts = shard_layer_weights(full[0].bfloat16(), full[1].bfloat16(), kw.bfloat16(), kb.bfloat16(), ow.bfloat16(),
+                              W, G, rank, world)
+    del full, kw, kb, ow
+    layers = {f: TPGretaConv(wts, W, G, True, 1e-6, world, None, None, fused=f) for f in (False, True)}
+    out = {"hidden": hidden, "channels_per_rank": wts.hi - wts.lo, "kernel_size": W, "group_size": G,
+           "ranks": world, "collective": "NCCL all-reduce of the out_proj partial sums" if world > 1 else None}
+    steps = max(5, min(args.steps, 50))
+    launches = 0
+    for name in ("decode", "prefill"):
+        g = torch.Generator().manual_seed(4000)
+        if name == "decode":
+            lengths = [1] * 256
+            n_slots = 1024
+        else:
+            lengths = make_prefill(torch, "cpu", 5000, D=8, W=W, G=8)["lengths"]
+            n_slots = 64
+        T, N = sum(lengths), len(lengths)
+        hs = torch.randn(T, hidden, generator=g).bfloat16().to(dev)
+        starts = torch.tensor([0] + _cumsum(lengths), dtype=torch.int32, device=dev)
+        slots = torch.randperm(n_slots, generator=g)[:N].to(torch.int32).to(dev)
+        init = torch.ones(N, dtype=torch.int8, device=dev)
+        state = torch.randn(n_slots, wts.hi - wts.lo, W - 1, generator=g).bfloat16().to(dev)
+        res = {"tokens": T}
+        for fused, layer in layers.items():
+            # a serving step replays the layer from a CUDA graph (as vLLM
+            # does), so the host's per-call Python and launch work is not
+            # timed; the all-reduce is captured with the rest
+            call = lambda _b, layer=layer: layer(hs, state, starts, slots, init)
+            sec = time_graph(torch, [None], call, steps, args.warmup, dist) / steps
+            res["fused_projection" if fused else "three_projections"] = dict(us=sec * 1e6, tokens_per_s=T / sec)
+            launches += steps
+        out[name] = res
+    out["launches"] = launches
     return out
 
 
@@ -910,7 +974,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--workload", choices=["prefill", "decode", "train", "greta", "hf", "all"], default="all")
+    ap.add_argument("--workload", choices=["prefill", "decode", "train", "greta", "hf", "tp", "all"], default="all")
     ap.add_argument("--shard", choices=["requests", "channels"], default="requests")
     ap.add_argument("--decode-steps", type=int, default=None)
     ap.add_argument("--train-steps", type=int, default=None)
@@ -1066,6 +1130,8 @@ def main():
             out["greta_layer"] = run_greta(torch, vc, dev, args, dist, rank, world, peak)
         if args.workload in ("hf", "all"):
             out["hf"] = run_hf(torch, dev, args, dist, rank, peak)
+        if args.workload in ("tp", "all"):
+            out["tp_layer"] = run_tp_layer(torch, dev, args, dist, rank, world)
         if world > 1 and args.shard == "requests" and args.workload in ("prefill", "all"):
             out["channel_split"] = run_channel_split(torch, vc, dev, args, dist, rank, world, peak)
         e2e = run_e2e_prefill(torch, vc, dev, args, dist) if args.workload in ("prefill", "all") else None
@@ -1104,6 +1170,9 @@ def main():
             hd = out["hf"]["headline"]["decode_rows"]
             head = dict(tokens_per_s=hd["tokens_per_s"], ms_per_step=hd["us"] / 1e3,
                         achieved_gbs=hd["bytes"] / hd["us"] / 1e3, frac=hd["frac"])
+        if head is None and set(out) == {"tp_layer"}:  # --workload tp: the fused decode layer leads
+            td = out["tp_layer"]["decode"]["fused_projection"]
+            head = dict(tokens_per_s=td["tokens_per_s"], ms_per_step=td["us"] / 1e3, achieved_gbs=None, frac=None)
         if head is None:  # a single non-prefill workload was asked for
             key = next(iter(out))
             head = out[key]
@@ -1129,7 +1198,7 @@ def main():
                          "frac": head["frac"], "traffic": head.get("traffic"),
                          "peak_source": f"{peak_kind} copy bandwidth (MEASURED_PEAKS.json hbm_gbs)"
                          if peak_kind == "measured" else "fallback 6.65 TB/s",
-                         "frac_of_8tbs_spec": head["achieved_gbs"] / 8000.0},
+                         "frac_of_8tbs_spec": None if head["achieved_gbs"] is None else head["achieved_gbs"] / 8000.0},
             "cpu_baseline": cpu,
             "e2e": None if e2e is None else {"value": e2e["tokens_per_s"] * scale, "unit": "tokens/s",
                                              "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"],

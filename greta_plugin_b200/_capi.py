@@ -95,6 +95,9 @@ def lib() -> ctypes.CDLL:
         getattr(L, f"greta_dynconv_{name}_ex").argtypes = args + [P]
         getattr(L, f"greta_dynconv_{name}").restype = I32
         getattr(L, f"greta_dynconv_{name}_ex").restype = I32
+    # packed_state with row strides: x, ldx, w, ldw, gate, ldg, then as packed_state from y on
+    L.greta_dynconv_packed_state_ld_ex.argtypes = [I32, P, I64, P, I64, P, I64] + sig["packed_state"][4:] + [P]
+    L.greta_dynconv_packed_state_ld_ex.restype = I32
     L.greta_dynconv_supports.argtypes = [I64, I64]
     L.greta_dynconv_device_errors.argtypes = [I32]
     L.greta_dynconv_status_string.argtypes = [I32]

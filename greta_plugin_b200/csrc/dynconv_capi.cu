@@ -71,13 +71,23 @@ LaunchShape make_shape(long long chunks, int64_t D, int nv, int tx, int ty) {
 
 int finish(cudaError_t e) { return e == cudaSuccess ? GRETA_OK : GRETA_ERR_LAUNCH; }
 
+// Row strides of the inputs: 0 means a contiguous tensor (x and gate rows of
+// D elements, filter rows of W * D/G).
+template <typename P>
+P with_strides(P p) {
+  if (p.ldx == 0) p.ldx = p.D;
+  if (p.ldg == 0) p.ldg = p.D;
+  if (p.ldw == 0) p.ldw = (long long)p.W * (p.D / p.G);
+  return p;
+}
+
 cudaError_t run_fwd(int dtype, const FwdParams& p, int nv, int norm, const LaunchShape& s, void* stream) {
   const int gv = group_vec(nv, p.G);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   switch (dtype) {
-    case GRETA_DT_F32: return launch_fwd_f32(p, nv, norm, gv, s, st);
-    case GRETA_DT_F16: return launch_fwd_f16(p, nv, norm, gv, s, st);
-    default: return launch_fwd_bf16(p, nv, norm, gv, s, st);
+    case GRETA_DT_F32: return launch_fwd_f32(with_strides(p), nv, norm, gv, s, st);
+    case GRETA_DT_F16: return launch_fwd_f16(with_strides(p), nv, norm, gv, s, st);
+    default: return launch_fwd_bf16(with_strides(p), nv, norm, gv, s, st);
   }
 }
 
@@ -95,18 +105,18 @@ cudaError_t run_fwd_decode(int dtype, const FwdParams& p, int norm, const Launch
   const int gv = group_vec(kVec, p.G);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   switch (dtype) {
-    case GRETA_DT_F32: return launch_fwd_decode_f32(p, norm, gv, s, st);
-    case GRETA_DT_F16: return launch_fwd_decode_f16(p, norm, gv, s, st);
-    default: return launch_fwd_decode_bf16(p, norm, gv, s, st);
+    case GRETA_DT_F32: return launch_fwd_decode_f32(with_strides(p), norm, gv, s, st);
+    case GRETA_DT_F16: return launch_fwd_decode_f16(with_strides(p), norm, gv, s, st);
+    default: return launch_fwd_decode_bf16(with_strides(p), norm, gv, s, st);
   }
 }
 
 cudaError_t run_fwd_wide(int dtype, const FwdParams& p, int norm, dim3 grid, dim3 block, int groups, void* stream) {
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   switch (dtype) {
-    case GRETA_DT_F32: return launch_fwd_wide_f32(p, norm, grid, block, groups, st);
-    case GRETA_DT_F16: return launch_fwd_wide_f16(p, norm, grid, block, groups, st);
-    default: return launch_fwd_wide_bf16(p, norm, grid, block, groups, st);
+    case GRETA_DT_F32: return launch_fwd_wide_f32(with_strides(p), norm, grid, block, groups, st);
+    case GRETA_DT_F16: return launch_fwd_wide_f16(with_strides(p), norm, grid, block, groups, st);
+    default: return launch_fwd_wide_bf16(with_strides(p), norm, grid, block, groups, st);
   }
 }
 
@@ -188,9 +198,9 @@ cudaError_t run_rows(int dtype, const RowsParams& p, int norm, int gv, dim3 grid
                      void* stream) {
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   switch (dtype) {
-    case GRETA_DT_F32: return launch_fwd_rows_f32(p, norm, gv, grid, block, smem, st);
-    case GRETA_DT_F16: return launch_fwd_rows_f16(p, norm, gv, grid, block, smem, st);
-    default: return launch_fwd_rows_bf16(p, norm, gv, grid, block, smem, st);
+    case GRETA_DT_F32: return launch_fwd_rows_f32(with_strides(p), norm, gv, grid, block, smem, st);
+    case GRETA_DT_F16: return launch_fwd_rows_f16(with_strides(p), norm, gv, grid, block, smem, st);
+    default: return launch_fwd_rows_bf16(with_strides(p), norm, gv, grid, block, smem, st);
   }
 }
 
@@ -209,9 +219,12 @@ int64_t slice_channels(int64_t D, int64_t max_c) {
 // it does not.
 int try_rows_fwd(int dtype, RowsParams p, bool gate, int norm, void* stream, const Opts& o) {
   if (o.kernel != GRETA_KERNEL_AUTO && o.kernel != GRETA_KERNEL_ROWS) return -1;
+  p = with_strides(p);
   p.wait_log2 = o.wait_log2;
   p.withhold = o.withhold;
   const int es = esize(dtype);
+  // every bulk copy starts on a 16-byte boundary: row strides too
+  if ((p.ldx * es) % 16 != 0 || (p.ldg * es) % 16 != 0 || (p.ldw * es) % 16 != 0) return -1;
   const int64_t D = p.D, W = p.W, G = p.G, DC = D / G;
   if (D % 256 != 0 || W > kMaxWGeneric) return -1;
   if (p.mode == kModePacked && p.nseq > kMaxSeqsTma) return -1;
@@ -542,6 +555,17 @@ int greta_dynconv_packed_state_ex(int dtype, const void* x, const void* w, const
                                   const int32_t* starts, const int32_t* slots, const int8_t* has_initial,
                                   int64_t num_reqs, int64_t T, int64_t D, int64_t W, int64_t G, int norm,
                                   float eps, int32_t* error_flags, void* stream, const greta_dynconv_options* opt) {
+  return greta_dynconv_packed_state_ld_ex(dtype, x, D, w, W * (G > 0 ? D / G : 0), gate, D, y, state, num_slots,
+                                          s_slot, s_d, s_h, starts, slots, has_initial, num_reqs, T, D, W, G, norm,
+                                          eps, error_flags, stream, opt);
+}
+
+int greta_dynconv_packed_state_ld_ex(int dtype, const void* x, int64_t ldx, const void* w, int64_t ldw,
+                                     const void* gate, int64_t ldg, void* y, void* state, int64_t num_slots,
+                                     int64_t s_slot, int64_t s_d, int64_t s_h, const int32_t* starts,
+                                     const int32_t* slots, const int8_t* has_initial, int64_t num_reqs, int64_t T,
+                                     int64_t D, int64_t W, int64_t G, int norm, float eps, int32_t* error_flags,
+                                     void* stream, const greta_dynconv_options* opt) {
   Opts o;
   int rc = parse_opts(opt, o);
   if (rc) return rc;
@@ -549,10 +573,17 @@ int greta_dynconv_packed_state_ex(int dtype, const void* x, const void* w, const
   if (rc) return rc;
   const int H = (int)W - 1;
   if (T < 0 || num_reqs < 0 || num_slots < 0) return GRETA_ERR_INVALID_ARG;
+  if (ldx < D || ldg < D || ldw < W * (D / G)) return GRETA_ERR_INVALID_ARG;
   if (T == 0 || num_reqs == 0) return GRETA_OK;  // empty tensors may have null pointers
   if (!x || !w || !y || !starts || !slots || !has_initial) return GRETA_ERR_INVALID_ARG;
   if (H > 0 && !state && num_slots > 0) return GRETA_ERR_INVALID_ARG;
-  const int nv = pick_nv(dtype, D, G, {x, gate, y}, w);
+  int nv = pick_nv(dtype, D, G, {x, gate, y}, w);
+  if (nv == kVec) {
+    // 16-byte vectors of x and gate rows, group vectors of filter rows
+    const int es = esize(dtype);
+    if ((ldx * es) % 16 != 0 || (gate != nullptr && (ldg * es) % 16 != 0) || ldw % group_vec(kVec, G) != 0)
+      nv = G > 32 ? 0 : 1;
+  }
   if (nv == 0) return GRETA_ERR_ALIGNMENT;
   const int es = esize(dtype);
   const bool decode_like = T <= 2 * num_reqs;
@@ -568,6 +599,7 @@ int greta_dynconv_packed_state_ex(int dtype, const void* x, const void* w, const
   p.initial = reinterpret_cast<const signed char*>(has_initial);
   p.err = error_flags;
   p.eps = eps;
+  p.ldx = ldx; p.ldg = ldg; p.ldw = ldw;
   if (H > 0 && state != nullptr && num_slots > 0) {
     p.state = state;
     p.s_slot = s_slot; p.s_d = s_d; p.s_h = s_h; p.num_slots = num_slots;
@@ -606,6 +638,7 @@ int greta_dynconv_packed_state_ex(int dtype, const void* x, const void* w, const
     tp.state = p.state; tp.s_slot = p.s_slot; tp.s_d = p.s_d; tp.s_h = p.s_h; tp.num_slots = p.num_slots;
     tp.st_layout = p.st_layout; tp.slots = slots; tp.initial = p.initial; tp.err = error_flags;
     tp.eps = eps;
+    tp.ldx = ldx; tp.ldg = ldg; tp.ldw = ldw;
     const int r = try_rows_fwd(dtype, tp, gate != nullptr, norm, stream, o);
     if (r >= 0) return r;
   }

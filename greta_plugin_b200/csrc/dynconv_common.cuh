@@ -56,6 +56,10 @@ struct FwdParams {
   const signed char* initial;  // [nseq] or null
   int* err;            // device error bits or null
   float eps;
+  // row strides (elements) of the inputs: x and gate rows (D when
+  // contiguous), filter rows (W * D/G when contiguous); outputs are
+  // contiguous [rows, D]
+  long long ldx, ldg, ldw;
 };
 
 struct BwdParams {
@@ -198,16 +202,30 @@ __device__ __forceinline__ float sigmoidf_(float v) { return __fdividef(1.f, 1.f
 // group reductions. NV channels per thread; GV groups per thread when G < NV
 // (GC = NV / GV channels each), else one group spread over lpg = G / NV lanes.
 // ---------------------------------------------------------------------------
-// The thread's part: out[gi] = sum of its GC channels of group gi, in order.
+// The thread's part: out[gi] = sum of its GC channels of group gi, in order;
+// eight channels as two halves of four, each summed in order, then added --
+// the sum that a thread of 4 channels and its neighbour lane form at the first
+// step of the butterfly below, so that kernels with 8 and with 4 channels per
+// thread give the same bits.
 template <int NV, int GV>
 __device__ __forceinline__ void group_local_sum(const float (&v)[NV], float (&out)[GV]) {
   constexpr int GC = NV / GV;
 #pragma unroll
   for (int gi = 0; gi < GV; ++gi) {
-    float s = 0.f;
+    if constexpr (GC == 8) {
+      float lo = 0.f, hi = 0.f;
 #pragma unroll
-    for (int c = 0; c < GC; ++c) s += v[gi * GC + c];
-    out[gi] = s;
+      for (int c = 0; c < 4; ++c) {
+        lo += v[gi * GC + c];
+        hi += v[gi * GC + 4 + c];
+      }
+      out[gi] = lo + hi;
+    } else {
+      float s = 0.f;
+#pragma unroll
+      for (int c = 0; c < GC; ++c) s += v[gi * GC + c];
+      out[gi] = s;
+    }
   }
 }
 

@@ -192,19 +192,19 @@ struct TokenLoads {
 template <typename T, int NV, int GV, int MAXW>
 __device__ __forceinline__ void load_token(TokenLoads<T, NV, GV, MAXW>& o, const T* __restrict__ xg,
                                            const T* __restrict__ wg, const T* __restrict__ gg, long long xrow,
-                                           long long orow, int D, int W, long long DC, long long f0, int d0,
-                                           bool active) {
+                                           long long orow, const FwdParams& p, int W, long long DC, long long f0,
+                                           int d0, bool active) {
   zero(o.x);
   zero(o.g);
 #pragma unroll
   for (int i = 0; i < MAXW; ++i) zero(o.w[i]);
   if (!active) return;
-  o.x = ld<T, NV>(xg + xrow * D + d0);
-  const T* wrow = wg + orow * W * DC + f0;
+  o.x = ld<T, NV>(xg + xrow * p.ldx + d0);
+  const T* wrow = wg + orow * p.ldw + f0;
 #pragma unroll
   for (int i = 0; i < MAXW; ++i)
     if (i < W) o.w[i] = ld<T, GV>(wrow + (long long)(W - 1 - i) * DC);
-  if (gg != nullptr) o.g = ld<T, NV>(gg + orow * D + d0);
+  if (gg != nullptr) o.g = ld<T, NV>(gg + orow * p.ldg + d0);
 }
 
 // A thread owns NV channels x a run of L consecutive tokens [rs, re) of one
@@ -253,7 +253,7 @@ __global__ void __launch_bounds__(256) dynconv_fwd_kernel(const FwdParams p) {
 
   // first token's operands: independent of the state, issued first
   TokenLoads<T, NV, GV, MAXW> nxt;
-  if (rs < re) load_token(nxt, xg, wg, gg, ci.x_base + rs, ci.o_base + rs, D, W, DC, f0, d0, active);
+  if (rs < re) load_token(nxt, xg, wg, gg, ci.x_base + rs, ci.o_base + rs, p, W, DC, f0, d0, active);
 
   const bool state_head = ci.hist == kHistState && ci.head && threadIdx.y == 0;
   const bool write_back = state_head && ci.slot >= 0 && active;
@@ -267,7 +267,7 @@ __global__ void __launch_bounds__(256) dynconv_fwd_kernel(const FwdParams p) {
 #pragma unroll
       for (int h = 0; h < MAXH; ++h) {
         zero(tail[h]);
-        if (h < H) tail[h] = ld<T, NV>(xg + (ci.x_base + ci.len - H + h) * D + d0);
+        if (h < H) tail[h] = ld<T, NV>(xg + (ci.x_base + ci.len - H + h) * p.ldx + d0);
       }
     }
     load_old_state<T, NV, WT, MAXH>(p, ci, d0, active, H, hw);
@@ -281,14 +281,14 @@ __global__ void __launch_bounds__(256) dynconv_fwd_kernel(const FwdParams p) {
       zero(hw[i]);
       if (i < H && active && rs < re) {
         const long long q = rs - 1 - i;
-        if (q >= 0 || ci.hist == kHistX) hw[i] = ld<T, NV>(xg + (ci.x_base + q) * D + d0);
+        if (q >= 0 || ci.hist == kHistX) hw[i] = ld<T, NV>(xg + (ci.x_base + q) * p.ldx + d0);
       }
     }
   }
 
   for (long long t = rs; t < re; ++t) {
     const TokenLoads<T, NV, GV, MAXW> cur = nxt;
-    if (t + 1 < re) load_token(nxt, xg, wg, gg, ci.x_base + t + 1, ci.o_base + t + 1, D, W, DC, f0, d0, active);
+    if (t + 1 < re) load_token(nxt, xg, wg, gg, ci.x_base + t + 1, ci.o_base + t + 1, p, W, DC, f0, d0, active);
     float acc[NV];
 #pragma unroll
     for (int c = 0; c < NV; ++c) acc[c] = 0.f;

@@ -139,7 +139,7 @@ __device__ __forceinline__ void decode_run(const FwdParams& p, long long row) {
     // shifted in place (greta/dynamic_conv.py:513-602); no metadata
     if (row >= p.nseq) return;
     const int r = (int)row;
-    load_token(tok, xg, wg, gg, r, r, D, W, DC, f0, d0, active);
+    load_token(tok, xg, wg, gg, r, r, p, W, DC, f0, d0, active);
     a = r;
     len = 1;
     c1 = 1;
@@ -150,7 +150,7 @@ __device__ __forceinline__ void decode_run(const FwdParams& p, long long row) {
   } else if (row < p.nseq) {
     const int r = (int)row;
     // speculative operands of token r, independent of the metadata
-    if (r < p.T) load_token(tok, xg, wg, gg, r, r, D, W, DC, f0, d0, active);
+    if (r < p.T) load_token(tok, xg, wg, gg, r, r, p, W, DC, f0, d0, active);
     a = (int)clampll(load_idx(p.starts, r, p.starts_i64), 0, p.T);
     int b = (int)clampll(load_idx(p.starts, r + 1, p.starts_i64), 0, p.T);
     const int slot_raw = p.slots != nullptr ? p.slots[r] : -1;
@@ -213,11 +213,11 @@ __device__ __forceinline__ void decode_run(const FwdParams& p, long long row) {
 #pragma unroll
     for (int i = 0; i < H; ++i) {
       zero(hw[i]);
-      if (active) hw[i] = ld<T, NV>(xg + (long long)(a + c0 - 1 - i) * D + d0);
+      if (active) hw[i] = ld<T, NV>(xg + (long long)(a + c0 - 1 - i) * p.ldx + d0);
     }
   }
   for (int t = c0; t < c1; ++t) {
-    if (!(spec && t == 0)) load_token(tok, xg, wg, gg, a + t, a + t, D, W, DC, f0, d0, active);
+    if (!(spec && t == 0)) load_token(tok, xg, wg, gg, a + t, a + t, p, W, DC, f0, d0, active);
     decode_token<T, NV, GV, W, NORM>(p, tok, [&](int c, int k) { return hw[H - 1 - k].v[c]; },
                                      yg + (long long)(a + t) * D + d0, active, lpg);
 #pragma unroll
@@ -237,7 +237,7 @@ __device__ __forceinline__ void decode_run(const FwdParams& p, long long row) {
     } else {
 #pragma unroll
       for (int h = 0; h < H; ++h) {
-        const PX v = ld<T, NV>(xg + (long long)(a + len - H + h) * D + d0);
+        const PX v = ld<T, NV>(xg + (long long)(a + len - H + h) * p.ldx + d0);
 #pragma unroll
         for (int c = 0; c < NV; ++c) set_slot_elem<DS>(nv, c, h, v.v[c]);
       }
@@ -255,10 +255,10 @@ __global__ void __launch_bounds__(128, decode_min_ctas<T>(W)) dynconv_fwd_decode
     // the row's operands, ahead of the wait (see below)
     const int d0 = ((int)(blockIdx.x % p.nblk) * blockDim.x + threadIdx.x) * kVec;
     if (d0 < p.D) {
-      prefetch_l2(reinterpret_cast<const T*>(p.x) + row * p.D + d0);
-      if (p.g != nullptr) prefetch_l2(reinterpret_cast<const T*>(p.g) + row * p.D + d0);
+      prefetch_l2(reinterpret_cast<const T*>(p.x) + row * p.ldx + d0);
+      if (p.g != nullptr) prefetch_l2(reinterpret_cast<const T*>(p.g) + row * p.ldg + d0);
       const long long DC = p.D / p.G;
-      const T* wr = reinterpret_cast<const T*>(p.w) + row * W * DC + d0 / p.G;
+      const T* wr = reinterpret_cast<const T*>(p.w) + row * p.ldw + d0 / p.G;
 #pragma unroll
       for (int k = 0; k < W; ++k) prefetch_l2(wr + k * DC);
     }
@@ -273,11 +273,11 @@ __global__ void __launch_bounds__(128, decode_min_ctas<T>(W)) dynconv_fwd_decode
       if (p.initial != nullptr) prefetch_l2(p.initial + row);
     }
     if (row < p.T && d0 < p.D) {
-      const T* xr = reinterpret_cast<const T*>(p.x) + row * p.D;
+      const T* xr = reinterpret_cast<const T*>(p.x) + row * p.ldx;
       prefetch_l2(xr + d0);
-      if (p.g != nullptr) prefetch_l2(reinterpret_cast<const T*>(p.g) + row * p.D + d0);
+      if (p.g != nullptr) prefetch_l2(reinterpret_cast<const T*>(p.g) + row * p.ldg + d0);
       const long long DC = p.D / p.G;
-      const T* wr = reinterpret_cast<const T*>(p.w) + row * W * DC + d0 / p.G;
+      const T* wr = reinterpret_cast<const T*>(p.w) + row * p.ldw + d0 / p.G;
 #pragma unroll
       for (int k = 0; k < W; ++k) prefetch_l2(wr + k * DC);
     }

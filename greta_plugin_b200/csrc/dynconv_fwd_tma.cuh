@@ -64,6 +64,9 @@ struct RowsParams {
   const signed char* initial;
   int* err;  // slot-range error bits (may be null)
   float eps;
+  // row strides (elements) of x and gate rows (D when contiguous) and of the
+  // filter rows (W * D/G when contiguous); y and yr are contiguous [U, D]
+  long long ldx, ldg, ldw;
   int wait_log2;  // pipeline wait bound: 2^wait_log2 polls (0 = default)
   int withhold;   // test hook: consumer warp 0 of CTA 0 keeps its first stage
   // shared-memory layout (bytes from the dynamic base): sequence offsets
@@ -225,17 +228,23 @@ __global__ void __launch_bounds__(32 + fwd_rows_max_channels(WT) / kVec, 1)
     // stage ring refills at L2 latency while HBM streams continuously.
     const long long u = min(nominal_start(p, range), p.U - 1);
     const unsigned n = (unsigned)min((long long)p.pf_rows, p.U - u);
-    const T* xs = reinterpret_cast<const T*>(p.x) + u * D;
-    const T* gs = p.g != nullptr ? reinterpret_cast<const T*>(p.g) + u * D : nullptr;
+    const T* xs = reinterpret_cast<const T*>(p.x) + u * p.ldx;
+    const T* gs = p.g != nullptr ? reinterpret_cast<const T*>(p.g) + u * p.ldg : nullptr;
     if (lane == 8 || (lane == 10 && gs != nullptr)) {
       const T* base = lane == 8 ? xs : gs;
-      if (p.nsplit == 1) {
+      const long long ld = lane == 8 ? p.ldx : p.ldg;
+      if (p.nsplit == 1 && ld == D) {
         bulk_prefetch_l2(base, n * (unsigned)(D * ES));
       } else {
-        for (unsigned j = 0; j < n; ++j) bulk_prefetch_l2(base + (long long)j * D + c0, (unsigned)(p.dcta * ES));
+        for (unsigned j = 0; j < n; ++j) bulk_prefetch_l2(base + (long long)j * ld + c0, (unsigned)(p.dcta * ES));
       }
     } else if (lane == 9) {
-      bulk_prefetch_l2(reinterpret_cast<const T*>(p.w) + u * W * DC, n * (unsigned)(W * DC * ES));
+      const T* wb = reinterpret_cast<const T*>(p.w) + u * p.ldw;
+      if (p.ldw == W * DC) {
+        bulk_prefetch_l2(wb, n * (unsigned)(W * DC * ES));
+      } else {
+        for (unsigned j = 0; j < n; ++j) bulk_prefetch_l2(wb + (long long)j * p.ldw, (unsigned)(W * DC * ES));
+      }
     } else if (lane == 11) {
       prefetch_l2(reinterpret_cast<const T*>(p.y) + u * D + c0);
     }
@@ -259,16 +268,20 @@ __global__ void __launch_bounds__(32 + fwd_rows_max_channels(WT) / kVec, 1)
   const unsigned rowx = (unsigned)(p.dcta * ES);
   const unsigned roww = p.wsplit ? (unsigned)(W * fct * ES) : (unsigned)(W * DC * ES);
   const unsigned sb0 = smem_addr(smem + p.off_stage);
-  const bool whole = p.nsplit == 1;  // slices are whole rows
+  // one copy for a stage's rows of a tensor when they are whole, contiguous
+  // rows; else a copy per row
+  const bool xwhole = p.nsplit == 1 && p.ldx == D;
+  const bool gwhole = p.nsplit == 1 && p.ldg == D;
+  const bool wwhole = p.ldw == W * DC;
 
   // Stage copies of tokens [t0, t0 + n) into the stage at shared address sb,
   // completing on mbarrier bar: x rows (not in CONTEXT mode, whose rows the
   // producer addresses per batch row), filters and gate rows.
   auto issue_x = [&](long long t0, int n, unsigned sb, unsigned bar) {
-    if (whole) {
+    if (xwhole) {
       bulk_g2s(sb, xg + t0 * D, (unsigned)n * rowx, bar);
     } else {
-      for (int j = 0; j < n; ++j) bulk_g2s(sb + j * rowx, xg + (t0 + j) * D + c0, rowx, bar);
+      for (int j = 0; j < n; ++j) bulk_g2s(sb + j * rowx, xg + (t0 + j) * p.ldx + c0, rowx, bar);
     }
   };
   auto issue_wg = [&](long long t0, int n, unsigned sb, unsigned bar) {
@@ -277,15 +290,17 @@ __global__ void __launch_bounds__(32 + fwd_rows_max_channels(WT) / kVec, 1)
       const long long fc0 = c0 >> p.log2g;
       for (int j = 0; j < n; ++j)
         for (int k = 0; k < W; ++k)
-          bulk_g2s(sb + p.so_w + j * roww + k * tapb, wg + ((t0 + j) * W + k) * DC + fc0, tapb, bar);
-    } else {
+          bulk_g2s(sb + p.so_w + j * roww + k * tapb, wg + (t0 + j) * p.ldw + k * DC + fc0, tapb, bar);
+    } else if (wwhole) {
       bulk_g2s(sb + p.so_w, wg + t0 * W * DC, (unsigned)n * roww, bar);
+    } else {
+      for (int j = 0; j < n; ++j) bulk_g2s(sb + p.so_w + j * roww, wg + (t0 + j) * p.ldw, roww, bar);
     }
     if (gg != nullptr) {
-      if (whole) {
+      if (gwhole) {
         bulk_g2s(sb + p.so_g, gg + t0 * D, (unsigned)n * rowx, bar);
       } else {
-        for (int j = 0; j < n; ++j) bulk_g2s(sb + p.so_g + j * rowx, gg + (t0 + j) * D + c0, rowx, bar);
+        for (int j = 0; j < n; ++j) bulk_g2s(sb + p.so_g + j * rowx, gg + (t0 + j) * p.ldg + c0, rowx, bar);
       }
     }
   };
@@ -298,14 +313,14 @@ __global__ void __launch_bounds__(32 + fwd_rows_max_channels(WT) / kVec, 1)
   // previous input rows a consumer thread needs first. They are loaded here,
   // before the sequence offsets arrive, and used if the guess was right.
   const long long u_spec = nominal_start(p, range);
-  Pack<T, kVec> hspec[MAXH];
+  Pack<T, NV> hspec[MAXH];
 #pragma unroll
   for (int i = 0; i < MAXH; ++i) zero(hspec[i]);
   if (threadIdx.x >= 32 && p.mode != kModeContext && u_spec >= H && u_spec <= p.U) {
-    const T* xs = reinterpret_cast<const T*>(p.x) + c0 + ((int)threadIdx.x - 32) * kVec;
+    const T* xs = reinterpret_cast<const T*>(p.x) + c0 + ((int)threadIdx.x - 32) * NV;
 #pragma unroll
     for (int i = 0; i < MAXH; ++i)
-      if (i < H) hspec[i] = ld<T, kVec>(xs + (u_spec - 1 - i) * D);
+      if (i < H) hspec[i] = ld<T, NV>(xs + (u_spec - 1 - i) * p.ldx);
   }
 
   if (p.mode == kModePacked) {
@@ -359,7 +374,7 @@ __global__ void __launch_bounds__(32 + fwd_rows_max_channels(WT) / kVec, 1)
       mbar_arrive_expect_tx(bar, (unsigned)n * (rowx + roww + (gg != nullptr ? rowx : 0u)));
       if (p.mode == kModeContext) {
         for (int j = 0; j < n; ++j) {
-          bulk_g2s(sb + j * rowx, xg + (cb * xrow_b + H + cq) * D + c0, rowx, bar);
+          bulk_g2s(sb + j * rowx, xg + (cb * xrow_b + H + cq) * p.ldx + c0, rowx, bar);
           if (++cq == (int)p.T) {
             cq = 0;
             ++cb;
@@ -440,7 +455,7 @@ __global__ void __launch_bounds__(32 + fwd_rows_max_channels(WT) / kVec, 1)
 #pragma unroll
       for (int h = 0; h < MAXH; ++h) {
         zero(taps[h]);
-        if (h < H) taps[h] = ld<T, NV>(xg + (rb - H + h) * D + d0);
+        if (h < H) taps[h] = ld<T, NV>(xg + (rb - H + h) * p.ldx + d0);
       }
       rows_store_taps<T, NV, WT, MAXH>(p, slot, d0, H, taps);
       slot = -1;  // written
@@ -451,7 +466,7 @@ __global__ void __launch_bounds__(32 + fwd_rows_max_channels(WT) / kVec, 1)
     if (p.mode == kModeContext) {
 #pragma unroll
       for (int i = 0; i < MAXH; ++i)
-        if (i < H) hw[i] = ld<T, NV>(xg + (b0 * xrow_b + H + q0 - 1 - i) * D + d0);
+        if (i < H) hw[i] = ld<T, NV>(xg + (b0 * xrow_b + H + q0 - 1 - i) * p.ldx + d0);
     } else {
       find_request(u0);
       if (u0 == ra) {
@@ -465,7 +480,7 @@ __global__ void __launch_bounds__(32 + fwd_rows_max_channels(WT) / kVec, 1)
         // mid-request start: the boundary rule guarantees u0 - ra >= W-1
 #pragma unroll
         for (int i = 0; i < MAXH; ++i)
-          if (i < H) hw[i] = ld<T, NV>(xg + (u0 - 1 - i) * D + d0);
+          if (i < H) hw[i] = ld<T, NV>(xg + (u0 - 1 - i) * p.ldx + d0);
       }
     }
   }
@@ -503,7 +518,7 @@ __global__ void __launch_bounds__(32 + fwd_rows_max_channels(WT) / kVec, 1)
         if (u != u0 && cq == 0) {  // a new batch row: its history is its context
 #pragma unroll
           for (int k = 0; k < MAXH; ++k)
-            if (k < H) hw[k] = ld<T, NV>(xg + (cb * xrow_b + H - 1 - k) * D + d0);
+            if (k < H) hw[k] = ld<T, NV>(xg + (cb * xrow_b + H - 1 - k) * p.ldx + d0);
         }
         if (++cq == (int)p.T) {  // position of the next token
           cq = 0;

@@ -58,7 +58,7 @@ __device__ __forceinline__ void block_sum_max(float& s, float& m) {
 template <typename T>
 __device__ __forceinline__ Pack<T, kVec> wide_input(const FwdParams& p, const ChunkInfo& ci, long long q, int d0,
                                                     int H) {
-  if (q >= 0) return ld<T, kVec>(reinterpret_cast<const T*>(p.x) + (ci.x_base + q) * p.D + d0);
+  if (q >= 0) return ld<T, kVec>(reinterpret_cast<const T*>(p.x) + (ci.x_base + q) * p.ldx + d0);
   Pack<T, kVec> v;
   zero(v);
   if (ci.has_state) {
@@ -103,7 +103,7 @@ __global__ void __launch_bounds__(kWideThreads) dynconv_fwd_wide_kernel(const Fw
     const long long orow = ci.o_base + t;
     T wk[kMaxWGeneric];
 #pragma unroll
-    for (int k = 0; k < kMaxWGeneric; ++k) wk[k] = k < W ? wg[(orow * W + k) * DC + f] : from_f<T>(0.f);
+    for (int k = 0; k < kMaxWGeneric; ++k) wk[k] = k < W ? wg[orow * p.ldw + k * DC + f] : from_f<T>(0.f);
     float scale = 1.f;
     if (NORM != kNormNone) {
       float ss = 0.f, mx = 0.f;
@@ -146,7 +146,7 @@ __global__ void __launch_bounds__(kWideThreads) dynconv_fwd_wide_kernel(const Fw
       float acc[kVec];
       wide_conv<T>(p, ci, t, d0, W, wk, acc);
       if (gg != nullptr) {
-        const Pack<T, kVec> gv = ld<T, kVec>(gg + orow * D + d0);
+        const Pack<T, kVec> gv = ld<T, kVec>(gg + orow * p.ldg + d0);
 #pragma unroll
         for (int c = 0; c < kVec; ++c) {
           const float gf = to_f(gv.v[c]);

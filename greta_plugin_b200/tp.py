@@ -184,11 +184,13 @@ class TPGretaConv(torch.nn.Module):
         filt = F.linear(hidden_states, self.w.kernel_proj, self.w.kernel_bias).view(T, self.kernel_size, self.filters)
         return x, filt, gate
 
-    def forward(self, hidden_states, state, starts, slots, has_initial):
+    def forward(self, hidden_states, state, starts, slots, has_initial, reduce: bool = True):
+        """The layer output; with reduce=False, this rank's out_proj partial
+        sum (the caller reduces)."""
         x, filt, gate = self.projections(hidden_states)
         mixed = self.conv(x, filt, gate, state, starts, slots, has_initial, self.group_size, self.norm, self.eps)
         y = F.linear(mixed, self.w.out_proj)
-        if self.world > 1:
+        if reduce and self.world > 1:
             import torch.distributed as dist
 
             dist.all_reduce(y, group=self.group)

@@ -29,6 +29,30 @@ def supports(group_size: int, channels: int) -> bool:
     return group_size > 0 and group_size & (group_size - 1) == 0 and channels % group_size == 0
 
 
+def _aligned_rows(t, row_stride):
+    return t.data_ptr() % 16 == 0 and (row_stride * t.element_size()) % 16 == 0
+
+
+def _rows(t, channels):
+    """A [T, D] input as (tensor, row stride): a view whose rows are
+    contiguous and 16-byte aligned (e.g. a column block of one projection
+    GEMM's output) is read in place, anything else is made contiguous."""
+    if t.stride(1) == 1 and t.stride(0) >= channels and _aligned_rows(t, t.stride(0)):
+        return t, t.stride(0)
+    return t.contiguous(), channels
+
+
+def _filter_rows(w):
+    """Filters [T, W, D/G] as (tensor, token-row stride): each token's W
+    filter rows must be contiguous (tap-major compact); the token rows may be
+    spaced (a column block of a concatenated projection output)."""
+    T, W, DC = w.shape
+    if w.stride(2) == 1 and (W == 1 or w.stride(1) == DC) and w.stride(0) >= W * DC and \
+            _aligned_rows(w, w.stride(0)):
+        return w, w.stride(0)
+    return w.contiguous(), W * DC
+
+
 def _launch(x, weights, gate, state, starts, slots, has_initial, group_size, norm, eps, out, flags):
     tokens, channels = x.shape
     width = weights.shape[1]
@@ -48,17 +72,22 @@ def _launch(x, weights, gate, state, starts, slots, has_initial, group_size, nor
         raise ValueError(f'Convolution cache dtype {state.dtype} must match x dtype {x.dtype}')
     if out.dtype != x.dtype or out.shape != x.shape or not out.is_contiguous():
         raise ValueError('out must be a contiguous tensor shaped and typed like x')
-    x = x.contiguous()
-    weights = weights.contiguous() if weights.dtype == x.dtype else weights.to(x.dtype).contiguous()
+    x, ldx = _rows(x, channels)
+    if weights.dtype != x.dtype:
+        weights = weights.to(x.dtype)
+    weights, ldw = _filter_rows(weights)
+    ldg = channels
     if gate is not None:
-        gate = gate.contiguous() if gate.dtype == x.dtype else gate.to(x.dtype).contiguous()
+        if gate.dtype != x.dtype:
+            gate = gate.to(x.dtype)
+        gate, ldg = _rows(gate, channels)
     starts = starts.to(device=x.device, dtype=torch.int32).contiguous()
     slots = slots.to(device=x.device, dtype=torch.int32).reshape(-1).contiguous()
     has_initial = has_initial.to(device=x.device, dtype=torch.int8).reshape(-1).contiguous()
     s_slot, s_d, s_h = state.stride()
     with torch.cuda.device(x.device.index):
-        st = _capi.lib().greta_dynconv_packed_state_ex(
-            _capi.dtype_code(x), _capi.ptr(x), _capi.ptr(weights), _capi.ptr(gate), _capi.ptr(out),
+        st = _capi.lib().greta_dynconv_packed_state_ld_ex(
+            _capi.dtype_code(x), _capi.ptr(x), ldx, _capi.ptr(weights), ldw, _capi.ptr(gate), ldg, _capi.ptr(out),
             _capi.ptr(state) if state.numel() else None, state.shape[0], s_slot, s_d, s_h, _capi.ptr(starts),
             _capi.ptr(slots), _capi.ptr(has_initial), slots.numel(), tokens, channels, width, group_size,
             _capi.NORM_STABLE if norm else _capi.NORM_NONE, float(eps), _capi.ptr(flags), _capi.stream_of(x),

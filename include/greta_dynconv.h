@@ -221,6 +221,26 @@ GRETA_API int greta_dynconv_packed_state_ex(int dtype, const void* x, const void
                                             const greta_dynconv_options* opt);
 
 /*
+ * greta_dynconv_packed_state with row strides for its inputs: ldx, ldg and ldw
+ * are the distances in elements between consecutive token rows of x, gate and
+ * the filters (x[t, d] at x + t*ldx + d, w[t, k, f] at w + t*ldw + k*(D/G) + f).
+ * With ldx = ldg = D and ldw = W*D/G it is greta_dynconv_packed_state. Strided
+ * inputs let x, gate and filters be column blocks of ONE projection GEMM's
+ * output [T, ld] (in_proj | gate_proj | kernel_proj concatenated), read in
+ * place instead of split into three tensors first. Requires ldx, ldg >= D,
+ * ldw >= W*D/G; the vector kernels also need 16-byte aligned rows. y stays
+ * contiguous [T, D]. No counterpart in the reference, which calls three
+ * separate projections (greta_vllm/model.py:115-124).
+ */
+GRETA_API int greta_dynconv_packed_state_ld_ex(int dtype, const void* x, int64_t ldx, const void* w, int64_t ldw,
+                                               const void* gate, int64_t ldg, void* y, void* state,
+                                               int64_t num_slots, int64_t s_slot, int64_t s_d, int64_t s_h,
+                                               const int32_t* starts, const int32_t* slots,
+                                               const int8_t* has_initial, int64_t num_reqs, int64_t T, int64_t D,
+                                               int64_t W, int64_t G, int norm, float eps, int32_t* error_flags,
+                                               void* stream, const greta_dynconv_options* opt);
+
+/*
  * Device-side error bits recorded by earlier kernels of this library on the
  * current device (bit 1, value 2: a pipeline wait of a row-streaming kernel
  * timed out and the kernel returned early, leaving part of its outputs
