@@ -589,6 +589,66 @@ def run_tp_layer(torch, dev, args, dist, rank, world):
     return out
 
 
+def run_train_layer(torch, dev, args, dist):
+    """Greta's conv layer in training (the HF path) at its defaults, hidden
+    2048, W = 7, G = 128, norm + gate, on 8 x 4096 packed tokens: forward and
+    backward of the three input projections, the conv and out_proj, as the
+    reference runs it (three GEMMs and their three backward GEMM pairs around
+    dynamic_causal_conv1d) and with the projections fused into one GEMM whose
+    output the conv reads in place and whose gradient the conv backward
+    writes in place (greta_plugin_b200.fused_layer). Plain launches between
+    events, max over ranks."""
+    from greta_plugin_b200 import dynamic_causal_conv1d
+    from greta_plugin_b200.fused_layer import FusedGretaConv
+
+    hidden, D, W, G = 2048, 2048, 7, 128
+    T = args.train_seqs * 4096
+    torch.manual_seed(99)
+
+    class Three(torch.nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.kernel_proj = torch.nn.Linear(hidden, (D // G) * W, bias=True)
+            self.gate_proj = torch.nn.Linear(hidden, D, bias=False)
+            self.in_proj = torch.nn.Linear(hidden, D, bias=False)
+            self.out_proj = torch.nn.Linear(D, hidden, bias=False)
+            self.kernel_size, self.group_size, self.norm, self.norm_eps = W, G, True, 1e-6
+
+        def forward(self, h, cu):
+            w = self.kernel_proj(h).view(h.shape[0], W, D // G)
+            y = dynamic_causal_conv1d(self.in_proj(h)[None], w, self.gate_proj(h)[None], cu, G, True, 1e-6)
+            return self.out_proj(y[0])
+
+    three = Three().to(device=dev, dtype=torch.bfloat16)
+    fused = FusedGretaConv.from_module(three)
+    gd = torch.Generator(device=dev).manual_seed(98)
+    h = (torch.randn(T, hidden, device=dev, generator=gd) * 0.5).bfloat16().requires_grad_()
+    dout = torch.randn(T, hidden, device=dev, generator=gd).bfloat16()
+    cu = torch.arange(0, T + 1, 4096, dtype=torch.int32, device=dev)
+    out = {"hidden": hidden, "channels": D, "kernel_size": W, "group_size": G, "tokens": T}
+    steps = max(3, min(args.train_steps, 10))
+    stream = torch.cuda.current_stream()
+    for name, layer in (("three_projections", three), ("fused_projection", fused)):
+        def step():
+            layer(h, cu).backward(dout)
+        for _ in range(max(args.warmup, 3)):
+            step()
+        torch.cuda.synchronize()
+        barrier(dist)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        hold_stream(torch, stream)
+        ev[0].record(stream)
+        for _ in range(steps):
+            step()
+        ev[1].record(stream)
+        torch.cuda.synchronize()
+        barrier(dist)
+        sec = reduce_max(torch, dist, ev[0].elapsed_time(ev[1]) / 1e3 / steps)
+        out[name] = dict(ms=sec * 1e3, tokens_per_s=T / sec)
+    out["launches"] = 2 * 2 * steps  # conv forward + backward per step, both forms
+    return out
+
+
 def run_reference_triton(torch, dev, args, dist, peak):
     """The reference's own GPU kernels (Triton, from baseline/_ref, stock code
     path) on the same B200, shapes and timing windows as the B200 kernels:
@@ -974,7 +1034,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--workload", choices=["prefill", "decode", "train", "greta", "hf", "tp", "all"], default="all")
+    ap.add_argument("--workload", choices=["prefill", "decode", "train", "greta", "hf", "tp", "layer", "all"],
+                    default="all")
     ap.add_argument("--shard", choices=["requests", "channels"], default="requests")
     ap.add_argument("--decode-steps", type=int, default=None)
     ap.add_argument("--train-steps", type=int, default=None)
@@ -1132,6 +1193,8 @@ def main():
             out["hf"] = run_hf(torch, dev, args, dist, rank, peak)
         if args.workload in ("tp", "all"):
             out["tp_layer"] = run_tp_layer(torch, dev, args, dist, rank, world)
+        if args.workload in ("layer", "all"):
+            out["train_layer"] = run_train_layer(torch, dev, args, dist)
         if world > 1 and args.shard == "requests" and args.workload in ("prefill", "all"):
             out["channel_split"] = run_channel_split(torch, vc, dev, args, dist, rank, world, peak)
         e2e = run_e2e_prefill(torch, vc, dev, args, dist) if args.workload in ("prefill", "all") else None
@@ -1170,6 +1233,9 @@ def main():
             hd = out["hf"]["headline"]["decode_rows"]
             head = dict(tokens_per_s=hd["tokens_per_s"], ms_per_step=hd["us"] / 1e3,
                         achieved_gbs=hd["bytes"] / hd["us"] / 1e3, frac=hd["frac"])
+        if head is None and set(out) == {"train_layer"}:  # --workload layer: the fused training layer leads
+            tl = out["train_layer"]["fused_projection"]
+            head = dict(tokens_per_s=tl["tokens_per_s"], ms_per_step=tl["ms"], achieved_gbs=None, frac=None)
         if head is None and set(out) == {"tp_layer"}:  # --workload tp: the fused decode layer leads
             td = out["tp_layer"]["decode"]["fused_projection"]
             head = dict(tokens_per_s=td["tokens_per_s"], ms_per_step=td["us"] / 1e3, achieved_gbs=None, frac=None)

@@ -98,6 +98,12 @@ def lib() -> ctypes.CDLL:
     # packed_state with row strides: x, ldx, w, ldw, gate, ldg, then as packed_state from y on
     L.greta_dynconv_packed_state_ld_ex.argtypes = [I32, P, I64, P, I64, P, I64] + sig["packed_state"][4:] + [P]
     L.greta_dynconv_packed_state_ld_ex.restype = I32
+    L.greta_dynconv_fwd_ld_ex.argtypes = [I32, P, I64, P, I64, P, I64, P, P, P, I32, I64, I64, I64, I64, I64, I32,
+                                          F, P, P]
+    L.greta_dynconv_fwd_ld_ex.restype = I32
+    L.greta_dynconv_bwd_ld_ex.argtypes = [I32, P, I64, P, I64, P, I64, P, P, P, I64, P, I64, P, I64, P, I32, I64,
+                                          I64, I64, I64, I64, I32, F, P, P]
+    L.greta_dynconv_bwd_ld_ex.restype = I32
     L.greta_dynconv_supports.argtypes = [I64, I64]
     L.greta_dynconv_device_errors.argtypes = [I32]
     L.greta_dynconv_status_string.argtypes = [I32]

@@ -87,7 +87,7 @@ __global__ void __launch_bounds__(256) dynconv_bwd_kernel(const BwdParams p) {
     zero(hw[i]);
     if (i < H && active) {
       const long long q = rs - 1 - i;
-      if (q >= 0) hw[i] = ld<T, NV>(xg + (ci.x_base + q) * D + d0);
+      if (q >= 0) hw[i] = ld<T, NV>(xg + (ci.x_base + q) * p.ldx + d0);
     }
   }
   float pend[MAXH][NV];  // pend[j] = partial dx of token (t - 1 - j)
@@ -100,7 +100,8 @@ __global__ void __launch_bounds__(256) dynconv_bwd_kernel(const BwdParams p) {
   for (long long t = rs; t < tend; ++t) {
     const bool own = t < re;
     const bool live = t < ci.len;  // dy is zero past the end of the sequence
-    const long long orow = (ci.o_base + t) * D + d0;
+    const long long orow = (ci.o_base + t) * D + d0;  // dout and yr (contiguous)
+    const long long trow = ci.o_base + t;
     Pack<T, NV> xr, dor, gr, yrr;
     Pack<T, GV> wr[MAXW];  // wr[i] = w[t, W-1-i]
     zero(xr);
@@ -110,11 +111,11 @@ __global__ void __launch_bounds__(256) dynconv_bwd_kernel(const BwdParams p) {
 #pragma unroll
     for (int i = 0; i < MAXW; ++i) zero(wr[i]);
     if (live && active) {
-      if (own) xr = ld<T, NV>(xg + (ci.x_base + t) * D + d0);
+      if (own) xr = ld<T, NV>(xg + (ci.x_base + t) * p.ldx + d0);
       dor = ld<T, NV>(dog + orow);
-      if (gg != nullptr) gr = ld<T, NV>(gg + orow);
+      if (gg != nullptr) gr = ld<T, NV>(gg + trow * p.ldg + d0);
       if (NORM != kNormNone) yrr = ld<T, NV>(yrg + orow);
-      const T* wrow = wg + (ci.o_base + t) * W * DC + f0;
+      const T* wrow = wg + trow * p.ldw + f0;
 #pragma unroll
       for (int i = 0; i < MAXW; ++i)
         if (i < W) wr[i] = ld<T, GV>(wrow + (long long)(W - 1 - i) * DC);
@@ -183,7 +184,7 @@ __global__ void __launch_bounds__(256) dynconv_bwd_kernel(const BwdParams p) {
             Pack<T, GV> o;
 #pragma unroll
             for (int gi = 0; gi < GV; ++gi) o.v[gi] = from_f<T>(s[gi]);
-            st<T, GV>(dwg + ((ci.o_base + t) * W + (W - 1 - i)) * DC + f0, o);
+            st<T, GV>(dwg + trow * p.lddw + (long long)(W - 1 - i) * DC + f0, o);
           }
         }
       }
@@ -196,7 +197,7 @@ __global__ void __launch_bounds__(256) dynconv_bwd_kernel(const BwdParams p) {
           const float hat = (NORM == kNormNone) ? yc[c] : to_f(yrr.v[c]) * rinv[c / GC];
           o.v[c] = from_f<T>(to_f(dor.v[c]) * hat * (sg * (1.f + gv * (1.f - sg))));
         }
-        st<T, NV>(dgg + orow, o);
+        st<T, NV>(dgg + trow * p.lddg + d0, o);
       }
     }
 
@@ -232,7 +233,7 @@ __global__ void __launch_bounds__(256) dynconv_bwd_kernel(const BwdParams p) {
       Pack<T, NV> o;
 #pragma unroll
       for (int c = 0; c < NV; ++c) o.v[c] = from_f<T>(done[c]);
-      st<T, NV>(dxg + (ci.x_base + tc) * D + d0, o);
+      st<T, NV>(dxg + (ci.x_base + tc) * p.lddx + d0, o);
     }
     if (own) {
 #pragma unroll

@@ -84,6 +84,9 @@ struct BwdRowsParams {
   int wait_log2;  // pipeline wait bound: 2^wait_log2 polls (0 = default)
   // shared-memory layout (bytes from the dynamic base)
   int off_bnd, off_stage, stage_bytes, so_w, so_do, so_g, so_yr;
+  // row strides (elements): inputs x, gate (D when contiguous) and filters
+  // (W * D/G); outputs dx, dg and dw likewise; yr and dout are contiguous
+  long long ldx, ldg, ldw, lddx, lddg, lddw;
 };
 
 template <typename T, int WT, int NORM, int GV>
@@ -160,13 +163,13 @@ __global__ void __launch_bounds__(bwd_rows_threads(WT, GV, bwd_rows_max_channels
   const unsigned per_row = 2u * rowx + roww + (gg != nullptr ? rowx : 0u) + (NORM != kNormNone ? rowx : 0u);
   // Issue tile i's copies into stage i % S (seen empty by the caller).
   auto issue = [&](long long i) {
-    const bool whole = p.nsplit == 1;  // slices are whole rows: one copy per tensor
-    // n rows of a [T, D] tensor's slice, starting at token t
-    auto copy_rows = [&](unsigned dst, const T* src, long long t, int n, unsigned bar) {
-      if (whole) {
+    // n rows (row stride ld) of a [T, D] tensor's slice, starting at token t:
+    // one copy when the slices are whole, contiguous rows, else one per row
+    auto copy_rows = [&](unsigned dst, const T* src, long long ld, long long t, int n, unsigned bar) {
+      if (p.nsplit == 1 && ld == D) {
         bulk_g2s(dst, src + t * D, (unsigned)n * rowx, bar);
       } else {
-        for (int j = 0; j < n; ++j) bulk_g2s(dst + j * rowx, src + (t + j) * D + c0, rowx, bar);
+        for (int j = 0; j < n; ++j) bulk_g2s(dst + j * rowx, src + (t + j) * ld + c0, rowx, bar);
       }
     };
     const int s = (int)(i % S);
@@ -175,18 +178,20 @@ __global__ void __launch_bounds__(bwd_rows_threads(WT, GV, bwd_rows_max_channels
     const unsigned bar = full0 + 8 * s;
     const unsigned sb = smem_addr(smem + p.off_stage) + (unsigned)(s * p.stage_bytes);
     mbar_arrive_expect_tx(bar, (unsigned)n * per_row);
-    copy_rows(sb, xg, t0, n, bar);
+    copy_rows(sb, xg, p.ldx, t0, n, bar);
     if (p.wsplit) {
       const unsigned tapb = (unsigned)(fct * ES);
       for (int j = 0; j < n; ++j)
         for (int k = 0; k < W; ++k)
-          bulk_g2s(sb + p.so_w + j * roww + k * tapb, wg + ((t0 + j) * W + k) * DC + c0 / G, tapb, bar);
-    } else {
+          bulk_g2s(sb + p.so_w + j * roww + k * tapb, wg + (t0 + j) * p.ldw + k * DC + c0 / G, tapb, bar);
+    } else if (p.ldw == W * DC) {
       bulk_g2s(sb + p.so_w, wg + t0 * W * DC, (unsigned)n * roww, bar);
+    } else {
+      for (int j = 0; j < n; ++j) bulk_g2s(sb + p.so_w + j * roww, wg + (t0 + j) * p.ldw, roww, bar);
     }
-    copy_rows(sb + p.so_do, dog, t0, n, bar);
-    if (gg != nullptr) copy_rows(sb + p.so_g, gg, t0, n, bar);
-    if (NORM != kNormNone) copy_rows(sb + p.so_yr, yrg, t0, n, bar);
+    copy_rows(sb + p.so_do, dog, D, t0, n, bar);
+    if (gg != nullptr) copy_rows(sb + p.so_g, gg, p.ldg, t0, n, bar);
+    if (NORM != kNormNone) copy_rows(sb + p.so_yr, yrg, D, t0, n, bar);
   };
   // bounded wait until the consumers have released the stage use of tile i
   const unsigned wlimit = wait_limit(p.wait_log2);
@@ -245,7 +250,7 @@ __global__ void __launch_bounds__(bwd_rows_threads(WT, GV, bwd_rows_max_channels
     find_request(u0);
 #pragma unroll
     for (int i = 0; i < MAXH; ++i)
-      if (i < H && u0 - 1 - i >= ra) hw[i] = ld<T, NV>(xg + (u0 - 1 - i) * D + d0);
+      if (i < H && u0 - 1 - i >= ra) hw[i] = ld<T, NV>(xg + (u0 - 1 - i) * p.ldx + d0);
   }
 
   // Store the complete dx rows pending at the end of a request (the last
@@ -259,7 +264,7 @@ __global__ void __launch_bounds__(bwd_rows_threads(WT, GV, bwd_rows_max_channels
         PX o;
 #pragma unroll
         for (int c = 0; c < NV; ++c) o.v[c] = from_f<T>(pend[j][c]);
-        st<T, NV>(dxg + v * D + d0, o);
+        st<T, NV>(dxg + v * p.lddx + d0, o);
       }
     }
   };
@@ -355,7 +360,7 @@ __global__ void __launch_bounds__(bwd_rows_threads(WT, GV, bwd_rows_max_channels
         float yc[NV];
 #pragma unroll
         for (int c = 0; c < NV; ++c) yc[c] = 0.f;
-        T* dwrow = dwg + u * W * DC + f0;
+        T* dwrow = dwg + u * p.lddw + f0;
         // GV == 1: this thread's part of the group's dw for the input i steps
         // back, summed over the group's lanes below (GV > 1: stored at once)
         float part[MAXP];
@@ -401,7 +406,7 @@ __global__ void __launch_bounds__(bwd_rows_threads(WT, GV, bwd_rows_max_channels
             const float hat = (NORM == kNormNone) ? yc[c] : to_f(yrr.v[c]) * rinv[c / GC];
             o.v[c] = from_f<T>(to_f(dor.v[c]) * hat * (sg * (1.f + gv * (1.f - sg))));
           }
-          st<T, NV>(dgg + u * D + d0, o);
+          st<T, NV>(dgg + u * p.lddg + d0, o);
         }
       }
 
@@ -440,7 +445,7 @@ __global__ void __launch_bounds__(bwd_rows_threads(WT, GV, bwd_rows_max_channels
         PX o;
 #pragma unroll
         for (int c = 0; c < NV; ++c) o.v[c] = from_f<T>(done[c]);
-        st<T, NV>(dxg + tc * D + d0, o);
+        st<T, NV>(dxg + tc * p.lddx + d0, o);
       }
 #pragma unroll
       for (int i = MAXH - 1; i > 0; --i) hw[i] = hw[i - 1];

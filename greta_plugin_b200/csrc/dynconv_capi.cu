@@ -57,6 +57,17 @@ int pick_nv(int dtype, int64_t D, int64_t G, std::initializer_list<const void*> 
   return 1;
 }
 
+// Row strides usable by the vector kernels: 16-byte rows for the [T, D]
+// tensors, whole group vectors for the filter rows.
+bool strides_vec_ok(int dtype, int64_t G, std::initializer_list<int64_t> rows, std::initializer_list<int64_t> wrows) {
+  const int es = esize(dtype);
+  for (int64_t ld : rows)
+    if ((ld * es) % 16 != 0) return false;
+  for (int64_t ld : wrows)
+    if (ld % group_vec(kVec, G) != 0) return false;
+  return true;
+}
+
 // 1-D grid of chunks x channel blocks, channel block fastest.
 LaunchShape make_shape(long long chunks, int64_t D, int nv, int tx, int ty) {
   const long long lanes = (D + nv - 1) / nv;
@@ -81,6 +92,16 @@ P with_strides(P p) {
   return p;
 }
 
+// The same for the backward's outputs dx, dg and dw.
+template <typename P>
+P with_bwd_strides(P p) {
+  p = with_strides(p);
+  if (p.lddx == 0) p.lddx = p.D;
+  if (p.lddg == 0) p.lddg = p.D;
+  if (p.lddw == 0) p.lddw = (long long)p.W * (p.D / p.G);
+  return p;
+}
+
 cudaError_t run_fwd(int dtype, const FwdParams& p, int nv, int norm, const LaunchShape& s, void* stream) {
   const int gv = group_vec(nv, p.G);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
@@ -95,9 +116,9 @@ cudaError_t run_bwd(int dtype, const BwdParams& p, int nv, int norm, const Launc
   const int gv = group_vec(nv, p.G);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   switch (dtype) {
-    case GRETA_DT_F32: return launch_bwd_f32(p, nv, norm, gv, s, st);
-    case GRETA_DT_F16: return launch_bwd_f16(p, nv, norm, gv, s, st);
-    default: return launch_bwd_bf16(p, nv, norm, gv, s, st);
+    case GRETA_DT_F32: return launch_bwd_f32(with_bwd_strides(p), nv, norm, gv, s, st);
+    case GRETA_DT_F16: return launch_bwd_f16(with_bwd_strides(p), nv, norm, gv, s, st);
+    default: return launch_bwd_bf16(with_bwd_strides(p), nv, norm, gv, s, st);
   }
 }
 
@@ -305,9 +326,9 @@ cudaError_t run_bwd_rows(int dtype, const BwdRowsParams& p, int norm, int gv, di
                          void* stream) {
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   switch (dtype) {
-    case GRETA_DT_F32: return launch_bwd_rows_f32(p, norm, gv, grid, block, smem, st);
-    case GRETA_DT_F16: return launch_bwd_rows_f16(p, norm, gv, grid, block, smem, st);
-    default: return launch_bwd_rows_bf16(p, norm, gv, grid, block, smem, st);
+    case GRETA_DT_F32: return launch_bwd_rows_f32(with_bwd_strides(p), norm, gv, grid, block, smem, st);
+    case GRETA_DT_F16: return launch_bwd_rows_f16(with_bwd_strides(p), norm, gv, grid, block, smem, st);
+    default: return launch_bwd_rows_bf16(with_bwd_strides(p), norm, gv, grid, block, smem, st);
   }
 }
 
@@ -318,8 +339,12 @@ cudaError_t run_bwd_rows(int dtype, const BwdRowsParams& p, int norm, int gv, di
 // saved pre-norm output). Returns -1 when it does not.
 int try_rows_bwd(int dtype, BwdRowsParams p, int norm, void* stream, const Opts& o) {
   if (o.kernel != GRETA_KERNEL_AUTO && o.kernel != GRETA_KERNEL_ROWS) return -1;
+  p = with_bwd_strides(p);
   p.wait_log2 = o.wait_log2;
   const int es = esize(dtype);
+  // bulk copies and vector stores start on 16-byte boundaries: row strides too
+  for (long long ld : {p.ldx, p.ldg, p.ldw, p.lddx, p.lddg})
+    if ((ld * es) % 16 != 0) return -1;
   const int64_t D = p.D, W = p.W, G = p.G, DC = D / G;
   if (D % 256 != 0 || W > kMaxWBwdRows) return -1;
   if (p.mode == kModePacked && p.nseq > kMaxSeqsTma) return -1;
@@ -402,15 +427,25 @@ int greta_dynconv_fwd_ex(int dtype, const void* x, const void* w, const void* ga
                          const void* cu_seqlens, int cu_seqlens_int64, int64_t num_seqs, int64_t T,
                          int64_t D, int64_t W, int64_t G, int norm, float eps, void* stream,
                          const greta_dynconv_options* opt) {
+  return greta_dynconv_fwd_ld_ex(dtype, x, D, w, W * (G > 0 ? D / G : 0), gate, D, y, yr, cu_seqlens,
+                                 cu_seqlens_int64, num_seqs, T, D, W, G, norm, eps, stream, opt);
+}
+
+int greta_dynconv_fwd_ld_ex(int dtype, const void* x, int64_t ldx, const void* w, int64_t ldw, const void* gate,
+                            int64_t ldg, void* y, void* yr, const void* cu_seqlens, int cu_seqlens_int64,
+                            int64_t num_seqs, int64_t T, int64_t D, int64_t W, int64_t G, int norm, float eps,
+                            void* stream, const greta_dynconv_options* opt) {
   Opts o;
   int rc = parse_opts(opt, o);
   if (rc) return rc;
   rc = check_common(dtype, D, W, G, norm);
   if (rc) return rc;
   if (T < 0 || (cu_seqlens && num_seqs < 0)) return GRETA_ERR_INVALID_ARG;
+  if (ldx < D || ldg < D || ldw < W * (D / G)) return GRETA_ERR_INVALID_ARG;
   if (T == 0 || (cu_seqlens && num_seqs == 0)) return GRETA_OK;  // empty tensors may have null pointers
   if (!x || !w || !y) return GRETA_ERR_INVALID_ARG;
-  const int nv = pick_nv(dtype, D, G, {x, gate, y, yr}, w);
+  int nv = pick_nv(dtype, D, G, {x, gate, y, yr}, w);
+  if (nv == kVec && !strides_vec_ok(dtype, G, {ldx, gate ? ldg : D}, {ldw})) nv = G > 32 ? 0 : 1;
   if (nv == 0) return GRETA_ERR_ALIGNMENT;
   if (nv == kVec) {
     RowsParams tp{};
@@ -420,6 +455,7 @@ int greta_dynconv_fwd_ex(int dtype, const void* x, const void* w, const void* ga
     tp.nseq = cu_seqlens ? num_seqs : 1;
     tp.T = T; tp.U = T; tp.D = (int)D; tp.W = (int)W; tp.G = (int)G;
     tp.eps = eps;
+    tp.ldx = ldx; tp.ldg = ldg; tp.ldw = ldw;
     const int r = try_rows_fwd(dtype, tp, gate != nullptr, norm, stream, o);
     if (r >= 0) return r;
   }
@@ -432,6 +468,7 @@ int greta_dynconv_fwd_ex(int dtype, const void* x, const void* w, const void* ga
   p.T = T; p.D = (int)D; p.W = (int)W; p.G = (int)G;
   p.L = sh.L; p.chunk = sh.L * sh.ty;
   p.eps = eps;
+  p.ldx = ldx; p.ldg = ldg; p.ldw = ldw;
   const long long chunks = cdiv(T, p.chunk) + (cu_seqlens ? num_seqs : 0);
   if (chunks * (D / 8 + 1) > INT_MAX) return GRETA_ERR_INVALID_ARG;
   return finish(run_fwd(dtype, p, nv, norm, make_shape(chunks, D, nv, sh.tx, sh.ty), stream));
@@ -441,6 +478,16 @@ int greta_dynconv_bwd_ex(int dtype, const void* x, const void* w, const void* ga
                          const void* dout, void* dx, void* dw, void* dg, const void* cu_seqlens,
                          int cu_seqlens_int64, int64_t num_seqs, int64_t T, int64_t D, int64_t W,
                          int64_t G, int norm, float eps, void* stream, const greta_dynconv_options* opt) {
+  const int64_t wr = W * (G > 0 ? D / G : 0);
+  return greta_dynconv_bwd_ld_ex(dtype, x, D, w, wr, gate, D, yr, dout, dx, D, dw, wr, dg, D, cu_seqlens,
+                                 cu_seqlens_int64, num_seqs, T, D, W, G, norm, eps, stream, opt);
+}
+
+int greta_dynconv_bwd_ld_ex(int dtype, const void* x, int64_t ldx, const void* w, int64_t ldw, const void* gate,
+                            int64_t ldg, const void* yr, const void* dout, void* dx, int64_t lddx, void* dw,
+                            int64_t lddw, void* dg, int64_t lddg, const void* cu_seqlens, int cu_seqlens_int64,
+                            int64_t num_seqs, int64_t T, int64_t D, int64_t W, int64_t G, int norm, float eps,
+                            void* stream, const greta_dynconv_options* opt) {
   Opts o;
   int rc = parse_opts(opt, o);
   if (rc) return rc;
@@ -448,12 +495,16 @@ int greta_dynconv_bwd_ex(int dtype, const void* x, const void* w, const void* ga
   if (rc) return rc;
   if (norm == GRETA_NORM_STABLE) return GRETA_ERR_UNSUPPORTED;
   if (T < 0 || (cu_seqlens && num_seqs < 0)) return GRETA_ERR_INVALID_ARG;
+  if (ldx < D || ldg < D || lddx < D || lddg < D || ldw < W * (D / G) || lddw < W * (D / G))
+    return GRETA_ERR_INVALID_ARG;
   if (T == 0 || (cu_seqlens && num_seqs == 0)) return GRETA_OK;  // empty tensors may have null pointers
   if (!x || !w || !dout || !dx || !dw) return GRETA_ERR_INVALID_ARG;
   if ((gate == nullptr) != (dg == nullptr)) return GRETA_ERR_INVALID_ARG;
   if (norm != GRETA_NORM_NONE && yr == nullptr) return GRETA_ERR_INVALID_ARG;
   int nv = pick_nv(dtype, D, G, {x, gate, yr, dout, dx, dg}, w);
   if (nv == kVec && !aligned(dw, (int64_t)group_vec(kVec, G) * esize(dtype))) nv = G > 32 ? 0 : 1;
+  if (nv == kVec && !strides_vec_ok(dtype, G, {ldx, gate ? ldg : D, lddx, gate ? lddg : D}, {ldw, lddw}))
+    nv = G > 32 ? 0 : 1;
   if (nv == 0) return GRETA_ERR_ALIGNMENT;
   if (nv == kVec) {
     BwdRowsParams tp{};
@@ -464,6 +515,7 @@ int greta_dynconv_bwd_ex(int dtype, const void* x, const void* w, const void* ga
     tp.nseq = cu_seqlens ? num_seqs : 1;
     tp.T = T; tp.D = (int)D; tp.W = (int)W; tp.G = (int)G;
     tp.eps = eps;
+    tp.ldx = ldx; tp.ldg = ldg; tp.ldw = ldw; tp.lddx = lddx; tp.lddg = lddg; tp.lddw = lddw;
     const int r = try_rows_bwd(dtype, tp, norm, stream, o);
     if (r >= 0) return r;
   }
@@ -477,6 +529,7 @@ int greta_dynconv_bwd_ex(int dtype, const void* x, const void* w, const void* ga
   p.T = T; p.D = (int)D; p.W = (int)W; p.G = (int)G;
   p.L = sh.L; p.chunk = sh.L * sh.ty;
   p.eps = eps;
+  p.ldx = ldx; p.ldg = ldg; p.ldw = ldw; p.lddx = lddx; p.lddg = lddg; p.lddw = lddw;
   const long long chunks = cdiv(T, p.chunk) + (cu_seqlens ? num_seqs : 0);
   if (chunks * (D / 8 + 1) > INT_MAX) return GRETA_ERR_INVALID_ARG;
   return finish(run_bwd(dtype, p, nv, norm, make_shape(chunks, D, nv, sh.tx, sh.ty), stream));
@@ -578,12 +631,7 @@ int greta_dynconv_packed_state_ld_ex(int dtype, const void* x, int64_t ldx, cons
   if (!x || !w || !y || !starts || !slots || !has_initial) return GRETA_ERR_INVALID_ARG;
   if (H > 0 && !state && num_slots > 0) return GRETA_ERR_INVALID_ARG;
   int nv = pick_nv(dtype, D, G, {x, gate, y}, w);
-  if (nv == kVec) {
-    // 16-byte vectors of x and gate rows, group vectors of filter rows
-    const int es = esize(dtype);
-    if ((ldx * es) % 16 != 0 || (gate != nullptr && (ldg * es) % 16 != 0) || ldw % group_vec(kVec, G) != 0)
-      nv = G > 32 ? 0 : 1;
-  }
+  if (nv == kVec && !strides_vec_ok(dtype, G, {ldx, gate ? ldg : D}, {ldw})) nv = G > 32 ? 0 : 1;
   if (nv == 0) return GRETA_ERR_ALIGNMENT;
   const int es = esize(dtype);
   const bool decode_like = T <= 2 * num_reqs;

@@ -81,6 +81,9 @@ struct BwdParams {
   int chunk;
   int nblk;  // channel blocks; blockIdx.x = chunk * nblk + channel block
   float eps;
+  // row strides (elements): inputs x, gate (D when contiguous) and filters
+  // (W * D/G); outputs dx, dg and dw likewise; yr and dout are contiguous
+  long long ldx, ldg, ldw, lddx, lddg, lddw;
 };
 
 // ---------------------------------------------------------------------------

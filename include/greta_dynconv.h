@@ -221,6 +221,31 @@ GRETA_API int greta_dynconv_packed_state_ex(int dtype, const void* x, const void
                                             const greta_dynconv_options* opt);
 
 /*
+ * greta_dynconv_fwd / greta_dynconv_bwd with row strides (elements between
+ * consecutive token rows): ldx, ldg, ldw for the inputs x, gate and filters,
+ * and in the backward lddx, lddg, lddw for the outputs dx, dg and dw (y, yr
+ * and dout stay contiguous [T, D]). With x, gate and filters the column
+ * blocks of ONE projection GEMM's output [T, ld] (in_proj | gate_proj |
+ * kernel_proj concatenated) and dx, dg, dw written into the matching column
+ * blocks of one gradient buffer, the three projections' backward is one
+ * GEMM for the hidden states' gradient and one for the weights'. Contiguous
+ * strides make these the plain calls. No counterpart in the reference, which
+ * runs three projections and their three backward GEMMs
+ * (greta/modeling_greta.py:452-459).
+ */
+GRETA_API int greta_dynconv_fwd_ld_ex(int dtype, const void* x, int64_t ldx, const void* w, int64_t ldw,
+                                      const void* gate, int64_t ldg, void* y, void* yr, const void* cu_seqlens,
+                                      int cu_seqlens_int64, int64_t num_seqs, int64_t T, int64_t D, int64_t W,
+                                      int64_t G, int norm, float eps, void* stream,
+                                      const greta_dynconv_options* opt);
+GRETA_API int greta_dynconv_bwd_ld_ex(int dtype, const void* x, int64_t ldx, const void* w, int64_t ldw,
+                                      const void* gate, int64_t ldg, const void* yr, const void* dout, void* dx,
+                                      int64_t lddx, void* dw, int64_t lddw, void* dg, int64_t lddg,
+                                      const void* cu_seqlens, int cu_seqlens_int64, int64_t num_seqs, int64_t T,
+                                      int64_t D, int64_t W, int64_t G, int norm, float eps, void* stream,
+                                      const greta_dynconv_options* opt);
+
+/*
  * greta_dynconv_packed_state with row strides for its inputs: ldx, ldg and ldw
  * are the distances in elements between consecutive token rows of x, gate and
  * the filters (x[t, d] at x + t*ldx + d, w[t, k, f] at w + t*ldw + k*(D/G) + f).
