@@ -237,10 +237,38 @@ __global__ void __launch_bounds__(bwd_rows_threads(WT, GV, bwd_rows_max_channels
     }
   };
 
-  PX hw[MAXH];           // hw[i] = input at (current token - 1 - i)
+  // The history window: hw[i] = input at (current token - 1 - i), in the I/O
+  // type, or in fp32 (F32WIN: the wide-filter CTAs, whose 255-register budget
+  // has room) so that each input is converted once instead of once per tap.
+  constexpr bool F32WIN = INL;
+  PX hw[F32WIN ? 1 : MAXH];
+  float hwf[F32WIN ? MAXH : 1][NV];
   float pend[MAXH][NV];  // pend[j] = partial dx of token (current token - 1 - j)
+  auto clear_window = [&]() {
 #pragma unroll
-  for (int i = 0; i < MAXH; ++i) zero(hw[i]);
+    for (int i = 0; i < (F32WIN ? 1 : MAXH); ++i) zero(hw[i]);
+#pragma unroll
+    for (int i = 0; i < (F32WIN ? MAXH : 1); ++i)
+#pragma unroll
+      for (int c = 0; c < NV; ++c) hwf[i][c] = 0.f;
+  };
+  // the input i >= 1 steps back, channel c, in fp32
+  auto past = [&](int i, int c) -> float {
+    if constexpr (F32WIN) {
+      return hwf[i - 1 < MAXH ? i - 1 : 0][c];
+    } else {
+      return to_f(hw[i - 1 < MAXH ? i - 1 : 0].v[c]);
+    }
+  };
+  auto set_past = [&](int i, const PX& v) {
+    if constexpr (F32WIN) {
+#pragma unroll
+      for (int c = 0; c < NV; ++c) hwf[i][c] = to_f(v.v[c]);
+    } else {
+      hw[i] = v;
+    }
+  };
+  clear_window();
 #pragma unroll
   for (int j = 0; j < MAXH; ++j)
 #pragma unroll
@@ -250,7 +278,7 @@ __global__ void __launch_bounds__(bwd_rows_threads(WT, GV, bwd_rows_max_channels
     find_request(u0);
 #pragma unroll
     for (int i = 0; i < MAXH; ++i)
-      if (i < H && u0 - 1 - i >= ra) hw[i] = ld<T, NV>(xg + (u0 - 1 - i) * p.ldx + d0);
+      if (i < H && u0 - 1 - i >= ra) set_past(i, ld<T, NV>(xg + (u0 - 1 - i) * p.ldx + d0));
   }
 
   // Store the complete dx rows pending at the end of a request (the last
@@ -297,8 +325,7 @@ __global__ void __launch_bounds__(bwd_rows_threads(WT, GV, bwd_rows_max_channels
       if (u >= rb) {  // the next request starts at u: finish the last one
         flush();
         find_request(u);
-#pragma unroll
-        for (int i = 0; i < MAXH; ++i) zero(hw[i]);
+        clear_window();
 #pragma unroll
         for (int q = 0; q < MAXH; ++q)
 #pragma unroll
@@ -368,14 +395,24 @@ __global__ void __launch_bounds__(bwd_rows_threads(WT, GV, bwd_rows_max_channels
         for (int i = MAXP - 1; i >= 0; --i) {
           part[i] = 0.f;
           if (i < W) {
-            const PX& xs = (i == 0) ? xr : hw[i > 0 && i - 1 < MAXH ? i - 1 : 0];
+            float xf[NV];
+#pragma unroll
+            for (int c = 0; c < NV; ++c) xf[c] = (i == 0) ? to_f(xr.v[c]) : past(i, c);
             float prod[NV], sm[GV];
 #pragma unroll
-            for (int c = 0; c < NV; c += 2)
-              mul2(prod[c], prod[c + 1], dy[c], dy[c + 1], to_f(xs.v[c]), to_f(xs.v[c + 1]));
+            for (int c = 0; c < NV; c += 2) mul2(prod[c], prod[c + 1], dy[c], dy[c + 1], xf[c], xf[c + 1]);
             if (NORM == kNormNone && gg != nullptr) {
+              // the conv recompute, one rounding per tap (fmaf of the converted
+              // values is the value fma_io gives on the I/O-type ones)
+              const PW& wi = wr[i < MAXW ? i : 0];
+              if constexpr (F32WIN) {
 #pragma unroll
-              for (int c = 0; c < NV; ++c) yc[c] = fma_io(xs.v[c], wr[i < MAXW ? i : 0].v[c / GC], yc[c]);
+                for (int c = 0; c < NV; ++c) yc[c] = fmaf(xf[c], to_f(wi.v[c / GC]), yc[c]);
+              } else {
+                const PX& xs = (i == 0) ? xr : hw[i > 0 && i - 1 < MAXH ? i - 1 : 0];
+#pragma unroll
+                for (int c = 0; c < NV; ++c) yc[c] = fma_io(xs.v[c], wi.v[c / GC], yc[c]);
+              }
             }
             group_local_sum<NV, GV>(prod, sm);
             if (GV == 1) {
@@ -391,7 +428,10 @@ __global__ void __launch_bounds__(bwd_rows_threads(WT, GV, bwd_rows_max_channels
         if (GV == 1) {  // one group over lpg lanes: reduce-scatter the W sums
           int base, cnt;
           group_sum_scatter<MAXP>(part, lpg, lane, base, cnt);
-          if ((cidx & (lpg - 1)) < min(lpg, MAXP)) {
+          if (lpg >= MAXP) {
+            // one total per lane: the group's lanes 0 .. MAXP-1 hold taps base
+            if ((cidx & (lpg - 1)) < MAXP && base < W) dwrow[(long long)(W - 1 - base) * DC] = from_f<T>(part[0]);
+          } else {
 #pragma unroll
             for (int j = 0; j < MAXP; ++j)
               if (j < cnt && base + j < W) dwrow[(long long)(W - 1 - base - j) * DC] = from_f<T>(part[j]);
@@ -447,9 +487,16 @@ __global__ void __launch_bounds__(bwd_rows_threads(WT, GV, bwd_rows_max_channels
         for (int c = 0; c < NV; ++c) o.v[c] = from_f<T>(done[c]);
         st<T, NV>(dxg + tc * p.lddx + d0, o);
       }
+      if constexpr (F32WIN) {
 #pragma unroll
-      for (int i = MAXH - 1; i > 0; --i) hw[i] = hw[i - 1];
-      hw[0] = xr;
+        for (int i = MAXH - 1; i > 0; --i)
+#pragma unroll
+          for (int c = 0; c < NV; ++c) hwf[i][c] = hwf[i - 1][c];
+      } else {
+#pragma unroll
+        for (int i = MAXH - 1; i > 0; --i) hw[i] = hw[i - 1];
+      }
+      set_past(0, xr);
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(empty0 + 8 * cur_s);
