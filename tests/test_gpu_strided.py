@@ -34,35 +34,37 @@ def fused_inputs(g, T, D, W, G, pad, dtype=torch.bfloat16):
     return (x, w, gate), (x.contiguous(), w.contiguous(), gate.contiguous())
 
 
-def batch(g, lengths, n_slots, D, W):
+def batch(g, lengths, n_slots, D, W, dtype=torch.bfloat16):
     N = len(lengths)
     starts = torch.tensor([0] + list(np.cumsum(lengths)), dtype=torch.int32, device=DEV)
     slots = torch.randperm(n_slots, generator=g)[:N].to(torch.int32)
     slots[::5] = -1
     init = (torch.arange(N) % 3 != 1).to(torch.int8)
-    state = rand(g, n_slots, D, W - 1).to(DEV)
+    state = rand(g, n_slots, D, W - 1, dtype=dtype).to(DEV)
     return starts, slots.to(DEV), init.to(DEV), state
 
 
 CASES = [
-    # lengths, D, W, G, pad, kernel family
-    ([37, 1, 90, 5, 200, 3], 1024, 4, 1, 0, "auto"),       # prefill-like: row streaming
-    ([37, 1, 90, 5, 200, 3], 1024, 4, 1, 8, "register"),
-    ([1] * 40 + [9], 2048, 7, 128, 8, "auto"),            # decode-like: decode kernel
-    ([1] * 40 + [9], 2048, 7, 128, 0, "register"),
-    ([60, 2, 33], 2048, 7, 128, 8, "auto"),                # Greta layer prefill
-    ([60, 2, 33], 2048, 7, 512, 8, "auto"),                # wide groups
-    ([17, 4], 512, 3, 8, 24, "auto"),
+    # lengths, D, W, G, pad, kernel family, dtype
+    ([37, 1, 90, 5, 200, 3], 1024, 4, 1, 0, "auto", torch.bfloat16),       # prefill-like: row streaming
+    ([37, 1, 90, 5, 200, 3], 1024, 4, 1, 8, "register", torch.bfloat16),
+    ([1] * 40 + [9], 2048, 7, 128, 8, "auto", torch.bfloat16),            # decode-like: decode kernel
+    ([1] * 40 + [9], 2048, 7, 128, 0, "register", torch.bfloat16),
+    ([60, 2, 33], 2048, 7, 128, 8, "auto", torch.bfloat16),                # Greta layer prefill
+    ([60, 2, 33], 2048, 7, 512, 8, "auto", torch.bfloat16),                # wide groups
+    ([17, 4], 512, 3, 8, 24, "auto", torch.bfloat16),
+    ([33, 1, 70], 512, 4, 16, 8, "auto", torch.float16),
+    ([1] * 12 + [40], 512, 7, 64, 4, "auto", torch.float32),
 ]
 
 
-@pytest.mark.parametrize("lengths,D,W,G,pad,kernel", CASES)
-def test_strided_inputs_give_the_contiguous_bits(lengths, D, W, G, pad, kernel):
+@pytest.mark.parametrize("lengths,D,W,G,pad,kernel,dtype", CASES)
+def test_strided_inputs_give_the_contiguous_bits(lengths, D, W, G, pad, kernel, dtype):
     g = torch.Generator().manual_seed(D + W + G + pad)
     T = sum(lengths)
-    (xs, ws, gs), (xc, wc, gc) = fused_inputs(g, T, D, W, G, pad)
+    (xs, ws, gs), (xc, wc, gc) = fused_inputs(g, T, D, W, G, pad, dtype)
     assert xs.stride(0) != D
-    starts, slots, init, state = batch(g, lengths, 64, D, W)
+    starts, slots, init, state = batch(g, lengths, 64, D, W, dtype)
     s1, s2 = state.clone(), state.clone()
     with _capi.launch_options(kernel=kernel):
         y1 = packed_dynamic_conv_triton(xc, wc, gc, s1, starts, slots, init, G, norm=True)
@@ -72,7 +74,7 @@ def test_strided_inputs_give_the_contiguous_bits(lengths, D, W, G, pad, kernel):
     yo, so = oracle.packed(xc.float().cpu().numpy(), wc.float().cpu().numpy(), gc.float().cpu().numpy(),
                            state.float().cpu().numpy(), starts.cpu().numpy(), slots.cpu().numpy(),
                            init.cpu().numpy(), G, oracle.NORM_STABLE)
-    assert_close(y2, yo, torch.bfloat16)
+    assert_close(y2, yo, dtype)
     assert np.array_equal(s2.float().cpu().numpy(), so)
 
 
