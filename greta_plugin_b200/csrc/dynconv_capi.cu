@@ -57,12 +57,14 @@ int pick_nv(int dtype, int64_t D, int64_t G, std::initializer_list<const void*> 
   return 1;
 }
 
-// Row strides usable by the vector kernels: 16-byte rows for the [T, D]
-// tensors, whole group vectors for the filter rows.
+// Row strides usable by the vector kernels: every row of a [T, D] tensor
+// starts on a whole kVec-element vector (a thread loads its kVec channels as
+// one aligned pack: 16 bytes for 16-bit types, 32 for fp32), every filter row
+// on a whole group vector.
 bool strides_vec_ok(int dtype, int64_t G, std::initializer_list<int64_t> rows, std::initializer_list<int64_t> wrows) {
-  const int es = esize(dtype);
+  (void)dtype;
   for (int64_t ld : rows)
-    if ((ld * es) % 16 != 0) return false;
+    if (ld % kVec != 0) return false;
   for (int64_t ld : wrows)
     if (ld % group_vec(kVec, G) != 0) return false;
   return true;

@@ -30,7 +30,10 @@ def supports(group_size: int, channels: int) -> bool:
 
 
 def _aligned_rows(t, row_stride):
-    return t.data_ptr() % 16 == 0 and (row_stride * t.element_size()) % 16 == 0
+    """Rows that start on whole 8-element vectors (the kernels load a
+    thread's 8 channels as one aligned pack: 16 bytes for 16-bit types, 32
+    for fp32)."""
+    return t.data_ptr() % (8 * t.element_size()) == 0 and row_stride % 8 == 0
 
 
 def _rows(t, channels):
