@@ -140,11 +140,71 @@ def install_hf(fused_cache_prefill: bool = True) -> list[str]:
     return done
 
 
-def install_vllm() -> list[str]:
-    """Route the vLLM plugin's packed conv to the B200 kernel."""
+def _concat_projection(layer):
+    """[in_proj | gate_proj | kernel_proj | zero rows] of a GretaConv layer,
+    rows padded to a multiple of 8 so that every row of the GEMM's output
+    starts on a whole 8-element vector, and the matching bias (kernel_proj's;
+    zeros elsewhere). Built once and rebuilt only when a weight changes."""
+    params = (layer.in_proj.weight, layer.gate_proj.weight, layer.kernel_proj.weight, layer.kernel_proj.bias)
+    key = tuple((t.data_ptr(), t._version) for t in params)
+    cached = getattr(layer, "_b200_projection", None)
+    if cached is not None and cached[0] == key:
+        return cached[1], cached[2]
+    D, nk = layer.in_proj.weight.shape[0], layer.kernel_proj.weight.shape[0]
+    rows = (2 * D + nk + 7) // 8 * 8
+    with torch.no_grad():
+        w = layer.in_proj.weight.new_zeros(rows, layer.in_proj.weight.shape[1])
+        w[:D] = layer.in_proj.weight
+        w[D:2 * D] = layer.gate_proj.weight
+        w[2 * D:2 * D + nk] = layer.kernel_proj.weight
+        b = layer.kernel_proj.bias.new_zeros(rows)
+        b[2 * D:2 * D + nk] = layer.kernel_proj.bias
+    layer._b200_projection = (key, w, b)
+    return w, b
+
+
+def _fused_projection_forward(original):
+    """GretaConv.forward (greta_vllm/model.py:115-124) with in_proj, gate_proj
+    and kernel_proj as ONE GEMM over the concatenated weights; x, gate and the
+    filters handed to the reference's own custom op (and from there to the
+    B200 packed kernel) are column views of that one output, which the kernel
+    reads in place through their row strides. Everything after the
+    projections -- the op, run_conv, the cache plumbing, out_proj -- is the
+    reference's."""
+    if getattr(original, "__greta_b200__", False):
+        return original
+
+    @functools.wraps(original)
+    def forward(self, hidden_states, positions):
+        w, b = _concat_projection(self)
+        n, D = hidden_states.shape[0], self.config.hidden_dim
+        W, F = self.config.kernel_size, self.config.num_conv_filters
+        cat = torch.nn.functional.linear(hidden_states, w, b)
+        x, gate = cat[:, :D], cat[:, D:2 * D]
+        weights = cat[:, 2 * D:2 * D + W * F].unflatten(1, (W, F))
+        mixed = torch.empty((n, D), dtype=cat.dtype, device=cat.device)
+        torch.ops.vllm.greta_dynamic_conv(x, weights, gate, positions, mixed, self.prefix)
+        return self.out_proj(mixed)
+
+    forward.__greta_b200__ = True
+    return forward
+
+
+def install_vllm(fused_projection: bool = False) -> list[str]:
+    """Route the vLLM plugin's packed conv to the B200 kernel. With
+    fused_projection, GretaConv.forward also computes its three input
+    projections as one GEMM whose output the kernel reads in place
+    (_fused_projection_forward); its rounding then differs from three
+    separate GEMMs' by the GEMM's summation order."""
     done = []
     for module_name, names in VLLM_NAMES.items():
         done += _rebind(module_name, names)
+    if fused_projection:
+        vm = importlib.import_module("greta_vllm.model")
+        if not hasattr(vm, "GretaConv"):
+            raise AttributeError("greta_vllm.model has no attribute 'GretaConv'; unexpected reference version")
+        vm.GretaConv.forward = _fused_projection_forward(vm.GretaConv.forward)
+        done.append("greta_vllm.model.GretaConv.forward")
     return done
 
 

@@ -245,6 +245,54 @@ def test_vllm_layer_forward_through_custom_op(num_k_heads):
             assert torch.equal(s_k[s], state0[s])
 
 
+def test_vllm_layer_fused_projection_through_custom_op():
+    """install_vllm(fused_projection=True): GretaConv.forward computes its
+    three projections as one GEMM and hands column views of its output to the
+    reference's custom op, which passes them (strided, not copied) to the
+    B200 kernel; against the same layer with three GEMMs on the B200 kernel.
+    Outputs within bf16 tolerance, the cache within one GEMM rounding, the
+    slots no request names untouched."""
+    rdc, mg, cg = rh.reference_modules()
+    vconv, vtc, vm = rh.vllm_reference_modules()
+    from greta_plugin_b200 import integration
+
+    cfg, layer, prefix = rh.make_vllm_conv(vm, cg, torch.bfloat16, DEV, 7, 16)
+    D = cfg.hidden_dim
+    md = rh.short_conv_metadata(vm, [3, 9, 1], [5, 40], [0, 12], [True, False], DEV)
+    pos = torch.tensor([11, 0, 30] + list(range(7, 12)) + list(range(40)) + [0, 0, 0], device=DEV)
+    g = torch.Generator().manual_seed(9)
+    hs = torch.randn(pos.numel(), D, generator=g).to(DEV, torch.bfloat16)
+    state0 = layer.kv_cache[0].clone()
+    seen = []
+    saved_fwd = vm.GretaConv.forward
+    with torch.no_grad(), rh.forward_context(vm, layer, prefix, md):
+        with rh.installed(vllm=True):
+            y_3 = layer(hs, pos)
+            s_3 = layer.kv_cache[0].clone()
+            layer.kv_cache[0].copy_(state0)
+            kernel = vm.packed_dynamic_conv_triton
+
+            def spy(x, weights, gate, *a, **k):
+                seen.append((x.is_contiguous(), weights.is_contiguous(), gate.is_contiguous()))
+                return kernel(x, weights, gate, *a, **k)
+
+            vm.packed_dynamic_conv_triton = spy
+            try:
+                integration.install_vllm(fused_projection=True)
+                vm.packed_dynamic_conv_triton = spy
+                y_f = layer(hs, pos)
+            finally:
+                vm.GretaConv.forward = saved_fwd
+        s_f = layer.kv_cache[0].clone()
+    assert seen == [(False, False, False)], seen  # column views of one GEMM output reached the kernel
+    close(y_f, y_3, torch.bfloat16)
+    torch.testing.assert_close(s_f.float(), s_3.float(), rtol=1e-2, atol=1e-2)
+    named = {3, 9, 1, 0, 12}
+    for s in range(state0.shape[0]):
+        if s not in named:
+            assert torch.equal(s_f[s], state0[s])
+
+
 def _packed_case(D, W, G, lengths, slots, n_slots, norm, gate_on, seed, layout):
     g = torch.Generator().manual_seed(seed)
     T = sum(lengths)

@@ -101,6 +101,36 @@ def test_vllm_layer_forward_on_cpu_is_the_torch_path():
     assert torch.equal(layer.kv_cache[0], state)
 
 
+def test_vllm_fused_projection_forward_on_cpu():
+    """install_vllm(fused_projection=True) replaces GretaConv.forward's three
+    projections by one GEMM whose column views go to the reference's custom op
+    (on CPU: its torch packed_dynamic_conv); output and cache equal the
+    reference forward's (fp32, the GEMMs' summation order aside)."""
+    rdc, mg, cg = rh.reference_modules()
+    vconv, vtc, vm = rh.vllm_reference_modules()
+    from greta_plugin_b200 import integration
+
+    cfg, layer, prefix = rh.make_vllm_conv(vm, cg, torch.float32, "cpu", 1, 8, hidden_dim=256)
+    md = rh.short_conv_metadata(vm, [3, 5], [4, 6], [0, 7], [True, False], "cpu")
+    pos = torch.tensor([5, 0] + list(range(2, 6)) + list(range(6)))
+    hs = torch.randn(12, 256, generator=torch.Generator().manual_seed(2))
+    state0 = layer.kv_cache[0].clone()
+    with torch.no_grad(), rh.forward_context(vm, layer, prefix, md):
+        y_ref = layer(hs, pos)
+        s_ref = layer.kv_cache[0].clone()
+        layer.kv_cache[0].copy_(state0)
+        saved = vm.GretaConv.forward
+        try:
+            with rh.installed(vllm=True):
+                integration.install_vllm(fused_projection=True)
+                assert getattr(vm.GretaConv.forward, "__greta_b200__", False)
+                y_f = layer(hs, pos)
+        finally:
+            vm.GretaConv.forward = saved
+    torch.testing.assert_close(y_f, y_ref, rtol=1e-5, atol=1e-5)
+    torch.testing.assert_close(layer.kv_cache[0], s_ref, rtol=1e-5, atol=1e-5)
+
+
 def test_harness_skips_cleanly_without_reference(monkeypatch, tmp_path):
     import conftest
 
