@@ -122,20 +122,80 @@ def _fused_cached_prefill(original):
     return forward
 
 
-def install_hf(fused_cache_prefill: bool = True) -> list[str]:
+def _fused_training_applies(module, hidden_states, past_key_values, use_cache):
+    """The reference forward's autograd branch (greta/modeling_greta.py:517-552:
+    no cache update, a gradient needed, CUDA, use_triton_kernels), with a group
+    size its training kernel takes (greta/dynamic_conv.py:136-155: at most 128)."""
+    if use_cache and past_key_values is not None:
+        return False
+    if hidden_states.ndim != 3 or not hidden_states.is_cuda or not module.config.use_triton_kernels:
+        return False
+    if not torch.is_grad_enabled() or not (hidden_states.requires_grad or
+                                           any(p.requires_grad for p in module.parameters())):
+        return False
+    if module.kernel_proj.bias is None or module.group_size > 128:
+        return False
+    return hidden_states.dtype == module.in_proj.weight.dtype
+
+
+def _fused_projection_training(original):
+    """GretaDynamicConv.forward whose training branch computes in_proj,
+    gate_proj and kernel_proj as ONE GEMM over their concatenated weights
+    (fused_layer.FusedProjConvFunction: the conv reads x, gate and filters in
+    place from that output, and its backward writes dx, dg and dw into one
+    gradient buffer, so that the projections' backward is one GEMM for the
+    hidden states' gradient and one for the weights'); the B batch rows run
+    as one packed call of B sequences. Autograd splits the concatenated
+    weights' gradient back into the module's own parameters. Every other case
+    runs the forward it wraps."""
+    if getattr(original, "__greta_b200_fused__", False):
+        return original
+
+    @functools.wraps(original)
+    def forward(self, hidden_states, past_key_values=None, use_cache=False, attention_mask=None):
+        if not _fused_training_applies(self, hidden_states, past_key_values, use_cache):
+            return original(self, hidden_states, past_key_values=past_key_values, use_cache=use_cache,
+                            attention_mask=attention_mask)
+        from .fused_layer import FusedProjConvFunction
+
+        B, Q, hidden = hidden_states.shape
+        if attention_mask is not None:
+            if attention_mask.ndim != 2 or attention_mask.shape != (B, Q):
+                raise ValueError("Convolution attention_mask must match [batch, query_length]")
+            hidden_states = hidden_states.masked_fill(~attention_mask.bool().unsqueeze(-1), 0)
+        D, nk = self.in_proj.weight.shape[0], self.kernel_proj.weight.shape[0]
+        pad = (2 * D + nk + 7) // 8 * 8 - (2 * D + nk)
+        proj = torch.cat([self.in_proj.weight, self.gate_proj.weight, self.kernel_proj.weight,
+                          self.in_proj.weight.new_zeros(pad, hidden)])
+        cu = torch.arange(0, B * Q + 1, Q, dtype=torch.int32, device=hidden_states.device)
+        y = FusedProjConvFunction.apply(hidden_states.reshape(B * Q, hidden), proj, self.kernel_proj.bias, cu, D,
+                                        self.kernel_size, self.group_size, self.norm, self.norm_eps)
+        return self.out_proj(y.view(B, Q, D))
+
+    forward.__greta_b200_fused__ = True
+    return forward
+
+
+def install_hf(fused_cache_prefill: bool = True, fused_projection: bool = False) -> list[str]:
     """Route the HF Transformers plugin's conv calls to the B200 kernels.
 
     With fused_cache_prefill, GretaDynamicConv.forward is also wrapped so
     that a prefill chunk continuing a cached sequence is one launch on the
-    cache's own state tensor (see _fused_cached_prefill)."""
+    cache's own state tensor (see _fused_cached_prefill). With
+    fused_projection, its training branch computes the three input
+    projections as one GEMM (see _fused_projection_training); its rounding
+    then differs from three separate GEMMs' by the GEMM's summation order."""
     done = _rebind("greta.dynamic_conv", DYNAMIC_CONV_NAMES)
     done += _rebind("greta.modeling_greta", HF_GLOBALS)
-    if fused_cache_prefill:
+    if fused_cache_prefill or fused_projection:
         mg = importlib.import_module("greta.modeling_greta")
         if not hasattr(mg, "GretaDynamicConv"):
             raise AttributeError("greta.modeling_greta has no attribute 'GretaDynamicConv'; "
                                  "unexpected reference version")
-        mg.GretaDynamicConv.forward = _fused_cached_prefill(mg.GretaDynamicConv.forward)
+        if fused_cache_prefill:
+            mg.GretaDynamicConv.forward = _fused_cached_prefill(mg.GretaDynamicConv.forward)
+        if fused_projection:
+            mg.GretaDynamicConv.forward = _fused_projection_training(mg.GretaDynamicConv.forward)
         done.append("greta.modeling_greta.GretaDynamicConv.forward")
     return done
 

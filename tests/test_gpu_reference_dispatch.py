@@ -96,6 +96,46 @@ def test_hf_training_autograd_through_reference_forward_bf16():
         assert e_got <= 1.25 * e_ref + 1e-3, (i, e_got, e_ref)
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_hf_training_fused_projection(dtype):
+    """install_hf(fused_projection=True): the reference forward's training
+    branch with the three projections as one GEMM (the conv reading and its
+    backward writing in place) against the same module on the B200 kernels
+    with three GEMMs: output, input gradient and every parameter's gradient,
+    with an attention mask."""
+    mg, (c_ref, m_ref), (c_k, m_k) = _twin_modules(dtype)
+    from greta_plugin_b200 import integration
+
+    g = torch.Generator().manual_seed(4)
+    h0 = torch.randn(2, 37, c_ref.hidden_dim, generator=g).to(DEV, dtype)
+    dy = torch.randn(2, 37, c_ref.hidden_dim, generator=g).to(DEV, dtype)
+    mask = torch.ones(2, 37, dtype=torch.bool, device=DEV)
+    mask[1, 30:] = False
+
+    def step(m, fused):
+        h = h0.clone().requires_grad_()
+        saved = mg.GretaDynamicConv.forward
+        try:
+            with rh.installed(hf=True):
+                if fused:
+                    integration.install_hf(fused_projection=True)
+                    assert getattr(mg.GretaDynamicConv.forward, "__greta_b200_fused__", False)
+                y = m(h, attention_mask=mask)
+                y.backward(dy)
+        finally:
+            mg.GretaDynamicConv.forward = saved
+        return [y, h.grad] + [p.grad for _, p in m.named_parameters()]
+
+    rdc, mg, cg = rh.reference_modules()
+    c2, m2 = rh.make_hf_conv(mg, cg, dtype, DEV, 0, True)  # a second kernel-path module, same weights
+    m2.load_state_dict(m_ref.state_dict())
+    three = step(m_k, False)
+    fused = step(m2, True)
+    bound = 1e-4 if dtype == torch.float32 else 1e-2  # summation order of one GEMM vs three
+    for i, (a, b) in enumerate(zip(fused, three)):
+        assert rel_err(a, b) < bound, (i, rel_err(a, b))
+
+
 def test_hf_inference_without_cache_with_mask():
     mg, (c_ref, m_ref), (c_k, m_k) = _twin_modules(torch.bfloat16)
     g = torch.Generator().manual_seed(4)
