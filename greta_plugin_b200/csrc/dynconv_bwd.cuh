@@ -172,14 +172,15 @@ __global__ void __launch_bounds__(256) dynconv_bwd_kernel(const BwdParams p) {
       for (int i = MAXW - 1; i >= 0; --i) {
         if (i < W) {
           const Pack<T, NV>& xs = (i == 0) ? xr : hw[i > 0 ? i - 1 : 0];
-          float prod[NV], s[GV];
+          float xf[NV], s[GV];
 #pragma unroll
           for (int c = 0; c < NV; ++c) {
-            const float xv = to_f(xs.v[c]);
-            prod[c] = __fmul_rn(dy[c], xv);  // not fused into the group sum below
+            xf[c] = to_f(xs.v[c]);
             if (NORM == kNormNone && gg != nullptr) yc[c] = fma_io(xs.v[c], wr[i].v[c / GC], yc[c]);
           }
-          group_sum<NV, GV>(prod, s, lpg);
+          // the thread's part of the group sum, then the butterfly over its lanes
+          group_local_dot<NV, GV>(dy, xf, s);
+          if (GV == 1) group_xlane_sum(s[0], lpg);
           if (dw_writer) {
             Pack<T, GV> o;
 #pragma unroll

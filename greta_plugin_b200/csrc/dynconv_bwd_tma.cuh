@@ -398,9 +398,8 @@ __global__ void __launch_bounds__(bwd_rows_threads(WT, GV, bwd_rows_max_channels
             float xf[NV];
 #pragma unroll
             for (int c = 0; c < NV; ++c) xf[c] = (i == 0) ? to_f(xr.v[c]) : past(i, c);
-            float prod[NV], sm[GV];
-#pragma unroll
-            for (int c = 0; c < NV; c += 2) mul2(prod[c], prod[c + 1], dy[c], dy[c + 1], xf[c], xf[c + 1]);
+            float sm[GV];
+            group_local_dot<NV, GV>(dy, xf, sm);
             if (NORM == kNormNone && gg != nullptr) {
               // the conv recompute, one rounding per tap (fmaf of the converted
               // values is the value fma_io gives on the I/O-type ones)
@@ -414,7 +413,6 @@ __global__ void __launch_bounds__(bwd_rows_threads(WT, GV, bwd_rows_max_channels
                 for (int c = 0; c < NV; ++c) yc[c] = fma_io(xs.v[c], wi.v[c / GC], yc[c]);
               }
             }
-            group_local_sum<NV, GV>(prod, sm);
             if (GV == 1) {
               part[i] = sm[0];
             } else {

@@ -232,6 +232,34 @@ __device__ __forceinline__ void group_local_sum(const float (&v)[NV], float (&ou
   }
 }
 
+// out[gi] = the sum over the GC channels of group gi of a[c] * b[c] (the
+// thread's part of a group dot product): channel pairs accumulate in the two
+// lanes of the packed fp32 pipe -- a product, then a fused multiply-add --
+// and the two lanes are added last; eight channels as two halves of four,
+// then added (group_local_sum's grouping).
+template <int NV, int GV>
+__device__ __forceinline__ void group_local_dot(const float (&a)[NV], const float (&b)[NV], float (&out)[GV]) {
+  constexpr int GC = NV / GV;
+#pragma unroll
+  for (int gi = 0; gi < GV; ++gi) {
+    const int c0 = gi * GC;
+    if constexpr (GC == 1) {
+      out[gi] = __fmul_rn(a[c0], b[c0]);
+    } else {
+      float s[GC >= 8 ? 2 : 1];
+#pragma unroll
+      for (int h = 0; h < (GC >= 8 ? 2 : 1); ++h) {
+        const int c = c0 + 4 * h;
+        float e, o;
+        mul2(e, o, a[c], a[c + 1], b[c], b[c + 1]);
+        if constexpr (GC >= 4) fma2(e, o, a[c + 2], a[c + 3], b[c + 2], b[c + 3]);
+        s[h] = e + o;
+      }
+      out[gi] = GC >= 8 ? s[0] + s[GC >= 8 ? 1 : 0] : s[0];
+    }
+  }
+}
+
 // The butterfly over the lpg lanes of a group: lane bit 0 first, own + partner
 // at each step (lpg is warp-uniform; the steps are unrolled so that the
 // reductions of independent values can interleave).
