@@ -129,37 +129,25 @@ __global__ void __launch_bounds__(256) dynconv_bwd_kernel(const BwdParams p) {
 #pragma unroll
     for (int gi = 0; gi < GV; ++gi) rinv[gi] = 0.f;
     if (live) {  // uniform across the warp
+      {
+        float dv[NV], gf[NV];
 #pragma unroll
-      for (int c = 0; c < NV; ++c) {
-        const float dv = to_f(dor.v[c]);
+        for (int c = 0; c < NV; ++c) {
+          dv[c] = to_f(dor.v[c]);
+          gf[c] = to_f(gr.v[c]);
+        }
         if (gg != nullptr) {
-          const float gv = to_f(gr.v[c]);
-          dy[c] = dv * gv * sigmoidf_(gv);
+          bwd_gate_dy<NV>(dv, gf, dy);
         } else {
-          dy[c] = dv;
+#pragma unroll
+          for (int c = 0; c < NV; ++c) dy[c] = dv[c];
         }
       }
       if (NORM == kNormPlain) {
-        // sum(yr^2) and sum(yr * dy) over the group in one interleaved
-        // reduction; sum(n * dy) = rinv * sum(yr * dy)
-        float sq[NV], py[NV], cs[GV];
+        float yf[NV];
 #pragma unroll
-        for (int c = 0; c < NV; ++c) {
-          const float yp = to_f(yrr.v[c]);
-          sq[c] = yp * yp;
-          py[c] = yp * dy[c];
-        }
-        group_sum2<NV, GV>(sq, py, rinv, cs, lpg);
-#pragma unroll
-        for (int gi = 0; gi < GV; ++gi) {
-          rinv[gi] = rsqrtf(rinv[gi] * inv_g + p.eps);
-          cs[gi] *= rinv[gi];
-        }
-#pragma unroll
-        for (int c = 0; c < NV; ++c) {
-          const float n = to_f(yrr.v[c]) * rinv[c / GC];
-          dy[c] = rinv[c / GC] * (dy[c] - n * (cs[c / GC] * inv_g));
-        }
+        for (int c = 0; c < NV; ++c) yf[c] = to_f(yrr.v[c]);
+        bwd_norm<NV, GV>(yf, dy, rinv, inv_g, p.eps, lpg);
       }
     }
 
@@ -190,14 +178,18 @@ __global__ void __launch_bounds__(256) dynconv_bwd_kernel(const BwdParams p) {
         }
       }
       if (gg != nullptr && active) {
-        Pack<T, NV> o;
+        float dv[NV], gf[NV], hat[NV], dgv[NV];
 #pragma unroll
         for (int c = 0; c < NV; ++c) {
-          const float gv = to_f(gr.v[c]);
-          const float sg = sigmoidf_(gv);
-          const float hat = (NORM == kNormNone) ? yc[c] : to_f(yrr.v[c]) * rinv[c / GC];
-          o.v[c] = from_f<T>(to_f(dor.v[c]) * hat * (sg * (1.f + gv * (1.f - sg))));
+          dv[c] = to_f(dor.v[c]);
+          gf[c] = to_f(gr.v[c]);
+          hat[c] = (NORM == kNormNone) ? yc[c] : to_f(yrr.v[c]);
         }
+        if (NORM != kNormNone) scale_pairs<NV, GV>(hat, rinv);  // the normed output yr * rinv
+        bwd_gate_dg<NV>(dv, gf, hat, dgv);
+        Pack<T, NV> o;
+#pragma unroll
+        for (int c = 0; c < NV; ++c) o.v[c] = from_f<T>(dgv[c]);
         st<T, NV>(dgg + trow * p.lddg + d0, o);
       }
     }

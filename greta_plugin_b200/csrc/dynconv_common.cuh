@@ -147,6 +147,12 @@ __device__ __forceinline__ void fma2(float& d0, float& d1, float a0, float a1, f
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(pack2(a0, a1)), "l"(pack2(b0, b1)), "l"(pack2(d0, d1)));
   unpack2(r, d0, d1);
 }
+// d[c] = a[c] + b[c] for c = 0, 1
+__device__ __forceinline__ void add2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
+  unsigned long long r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(pack2(a0, a1)), "l"(pack2(b0, b1)));
+  unpack2(r, d0, d1);
+}
 // d[c] = a[c] * b[c] for c = 0, 1
 __device__ __forceinline__ void mul2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
   unsigned long long r;
@@ -216,12 +222,10 @@ __device__ __forceinline__ void group_local_sum(const float (&v)[NV], float (&ou
 #pragma unroll
   for (int gi = 0; gi < GV; ++gi) {
     if constexpr (GC == 8) {
+      // the two halves in the two lanes of the packed fp32 pipe
       float lo = 0.f, hi = 0.f;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        lo += v[gi * GC + c];
-        hi += v[gi * GC + 4 + c];
-      }
+      for (int c = 0; c < 4; ++c) add2(lo, hi, lo, hi, v[gi * GC + c], v[gi * GC + 4 + c]);
       out[gi] = lo + hi;
     } else {
       float s = 0.f;
@@ -391,6 +395,47 @@ __device__ __forceinline__ void stable_finish(float (&acc)[NV], float (&mx)[GV],
   for (int c = 0; c < NV; ++c) acc[c] *= ss[c / GC];
 }
 
+// q[c] = a[c] * a[c], channel pairs on the packed fp32 pipe (each lane
+// rounded like the scalar product)
+template <int NV>
+__device__ __forceinline__ void sq_pairs(const float (&a)[NV], float (&q)[NV]) {
+  if constexpr (NV % 2 == 0) {
+#pragma unroll
+    for (int c = 0; c < NV; c += 2) mul2(q[c], q[c + 1], a[c], a[c + 1], a[c], a[c + 1]);
+  } else {
+#pragma unroll
+    for (int c = 0; c < NV; ++c) q[c] = a[c] * a[c];
+  }
+}
+// a[c] *= s[group of c], channel pairs on the packed fp32 pipe
+template <int NV, int GV>
+__device__ __forceinline__ void scale_pairs(float (&a)[NV], const float (&s)[GV]) {
+  constexpr int GC = NV / GV;
+  if constexpr (NV % 2 == 0) {
+#pragma unroll
+    for (int c = 0; c < NV; c += 2) mul2(a[c], a[c + 1], a[c], a[c + 1], s[c / GC], s[(c + 1) / GC]);
+  } else {
+#pragma unroll
+    for (int c = 0; c < NV; ++c) a[c] *= s[c / GC];
+  }
+}
+// a[c] *= g[c] * sigmoid(g[c]) (the SiLU gate), the two products on the
+// packed fp32 pipe
+template <int NV>
+__device__ __forceinline__ void gate_pairs(float (&a)[NV], const float (&g)[NV]) {
+  if constexpr (NV % 2 == 0) {
+#pragma unroll
+    for (int c = 0; c < NV; c += 2) {
+      float t0, t1;
+      mul2(t0, t1, g[c], g[c + 1], sigmoidf_(g[c]), sigmoidf_(g[c + 1]));
+      mul2(a[c], a[c + 1], a[c], a[c + 1], t0, t1);
+    }
+  } else {
+#pragma unroll
+    for (int c = 0; c < NV; ++c) a[c] = a[c] * (g[c] * sigmoidf_(g[c]));
+  }
+}
+
 // Group RMS norm of a thread's NV accumulators, in place.
 //   plain : y * 1/sqrt(mean(y^2) + eps)               (greta/dynamic_conv.py:251-255)
 //   stable: s = max(max|y|, 1); y / (s * sqrt(mean((y/s)^2) + eps/s^2))
@@ -400,17 +445,14 @@ __device__ __forceinline__ void stable_finish(float (&acc)[NV], float (&mx)[GV],
 // (where a fast reciprocal flushes to zero) stay finite.
 template <int NORM, int NV, int GV>
 __device__ __forceinline__ void apply_norm(float (&acc)[NV], int G, int lpg, float eps) {
-  constexpr int GC = NV / GV;
   const float inv_g = 1.f / (float)G;  // G is a power of two: exact
   if (NORM == kNormPlain) {
     float sq[NV], ss[GV];
-#pragma unroll
-    for (int c = 0; c < NV; ++c) sq[c] = acc[c] * acc[c];
+    sq_pairs<NV>(acc, sq);
     group_sum<NV, GV>(sq, ss, lpg);
 #pragma unroll
     for (int gi = 0; gi < GV; ++gi) ss[gi] = rsqrtf(ss[gi] * inv_g + eps);
-#pragma unroll
-    for (int c = 0; c < NV; ++c) acc[c] *= ss[c / GC];
+    scale_pairs<NV, GV>(acc, ss);
   } else if (NORM == kNormStable) {
     float ab[NV], sq[NV], mx[GV], ss[GV];
 #pragma unroll
@@ -481,26 +523,19 @@ __device__ __forceinline__ void group_max_sum2(const float (&a)[NV], const float
 
 template <int NORM, int NV, int GV>
 __device__ __forceinline__ void apply_norm2(float (&a)[NV], float (&b)[NV], int G, int lpg, float eps) {
-  constexpr int GC = NV / GV;
   const float inv_g = 1.f / (float)G;  // G is a power of two: exact
   if (NORM == kNormPlain) {
     float qa[NV], qb[NV], sa[GV], sb[GV];
-#pragma unroll
-    for (int c = 0; c < NV; ++c) {
-      qa[c] = a[c] * a[c];
-      qb[c] = b[c] * b[c];
-    }
+    sq_pairs<NV>(a, qa);
+    sq_pairs<NV>(b, qb);
     group_sum2<NV, GV>(qa, qb, sa, sb, lpg);
 #pragma unroll
     for (int gi = 0; gi < GV; ++gi) {
       sa[gi] = rsqrtf(sa[gi] * inv_g + eps);
       sb[gi] = rsqrtf(sb[gi] * inv_g + eps);
     }
-#pragma unroll
-    for (int c = 0; c < NV; ++c) {
-      a[c] *= sa[c / GC];
-      b[c] *= sb[c / GC];
-    }
+    scale_pairs<NV, GV>(a, sa);
+    scale_pairs<NV, GV>(b, sb);
   } else if (NORM == kNormStable) {
     float ba[NV], bb[NV], qa[NV], qb[NV], ma[GV], mb[GV], sa[GV], sb[GV];
 #pragma unroll
@@ -513,6 +548,100 @@ __device__ __forceinline__ void apply_norm2(float (&a)[NV], float (&b)[NV], int 
     group_max_sum2<NV, GV>(ba, qa, bb, qb, ma, sa, mb, sb, lpg);
     stable_finish<NV, GV>(a, ma, sa, G, lpg, eps);
     stable_finish<NV, GV>(b, mb, sb, G, lpg, eps);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Backward pieces shared by both backward kernels, so that they stay
+// bit-identical: channel pairs on the packed fp32 pipe, each lane rounded
+// like the scalar operation.
+// ---------------------------------------------------------------------------
+// dy[c] = (dout[c] * g[c]) * sigmoid(g[c]): the gradient through the SiLU gate
+template <int NV>
+__device__ __forceinline__ void bwd_gate_dy(const float (&dv)[NV], const float (&g)[NV], float (&dy)[NV]) {
+  if constexpr (NV % 2 == 0) {
+#pragma unroll
+    for (int c = 0; c < NV; c += 2) {
+      float t0, t1;
+      mul2(t0, t1, dv[c], dv[c + 1], g[c], g[c + 1]);
+      mul2(dy[c], dy[c + 1], t0, t1, sigmoidf_(g[c]), sigmoidf_(g[c + 1]));
+    }
+  } else {
+#pragma unroll
+    for (int c = 0; c < NV; ++c) dy[c] = __fmul_rn(__fmul_rn(dv[c], g[c]), sigmoidf_(g[c]));
+  }
+}
+
+// The plain group RMS norm's backward, in place on dy, from the saved
+// pre-norm output yr: rinv = 1/sqrt(mean(yr^2) + eps), n = yr * rinv,
+// dy <- rinv * (dy - n * mean(n * dy)), where mean(n * dy) =
+// rinv * mean(yr * dy), so the two group sums (yr^2, yr * dy) run as one
+// interleaved reduction. Leaves rinv of each group.
+template <int NV, int GV>
+__device__ __forceinline__ void bwd_norm(const float (&yr)[NV], float (&dy)[NV], float (&rinv)[GV], float inv_g,
+                                         float eps, int lpg) {
+  constexpr int GC = NV / GV;
+  float sq[NV], py[NV], nk[GV];
+  if constexpr (NV % 2 == 0) {
+#pragma unroll
+    for (int c = 0; c < NV; c += 2) {
+      mul2(sq[c], sq[c + 1], yr[c], yr[c + 1], yr[c], yr[c + 1]);
+      mul2(py[c], py[c + 1], yr[c], yr[c + 1], dy[c], dy[c + 1]);
+    }
+  } else {
+#pragma unroll
+    for (int c = 0; c < NV; ++c) {
+      sq[c] = __fmul_rn(yr[c], yr[c]);
+      py[c] = __fmul_rn(yr[c], dy[c]);
+    }
+  }
+  group_sum2<NV, GV>(sq, py, rinv, nk, lpg);
+#pragma unroll
+  for (int gi = 0; gi < GV; ++gi) {
+    rinv[gi] = rsqrtf(rinv[gi] * inv_g + eps);
+    nk[gi] = -((nk[gi] * rinv[gi]) * inv_g);  // -mean(n * dy)
+  }
+  if constexpr (NV % 2 == 0) {
+#pragma unroll
+    for (int c = 0; c < NV; c += 2) {
+      const float r0 = rinv[c / GC], r1 = rinv[(c + 1) / GC];
+      float n0, n1, t0 = dy[c], t1 = dy[c + 1];
+      mul2(n0, n1, yr[c], yr[c + 1], r0, r1);
+      fma2(t0, t1, n0, n1, nk[c / GC], nk[(c + 1) / GC]);
+      mul2(dy[c], dy[c + 1], r0, r1, t0, t1);
+    }
+  } else {
+#pragma unroll
+    for (int c = 0; c < NV; ++c) {
+      const float r = rinv[c / GC];
+      dy[c] = __fmul_rn(r, __fmaf_rn(__fmul_rn(yr[c], r), nk[c / GC], dy[c]));
+    }
+  }
+}
+
+// dg[c] = (dout[c] * hat[c]) * (s * (1 + g[c] * (1 - s))), s = sigmoid(g[c]):
+// the gate's gradient, hat the gated value (the normed or plain conv output)
+template <int NV>
+__device__ __forceinline__ void bwd_gate_dg(const float (&dv)[NV], const float (&g)[NV], const float (&hat)[NV],
+                                            float (&dg)[NV]) {
+  if constexpr (NV % 2 == 0) {
+#pragma unroll
+    for (int c = 0; c < NV; c += 2) {
+      const float s0 = sigmoidf_(g[c]), s1 = sigmoidf_(g[c + 1]);
+      float o0 = 1.f, o1 = 1.f, q0 = 1.f, q1 = 1.f, a0, a1;
+      fma2(o0, o1, -1.f, -1.f, s0, s1);  // 1 - s
+      fma2(q0, q1, g[c], g[c + 1], o0, o1);
+      mul2(q0, q1, s0, s1, q0, q1);
+      mul2(a0, a1, dv[c], dv[c + 1], hat[c], hat[c + 1]);
+      mul2(dg[c], dg[c + 1], a0, a1, q0, q1);
+    }
+  } else {
+#pragma unroll
+    for (int c = 0; c < NV; ++c) {
+      const float sg = sigmoidf_(g[c]);
+      const float q = __fmul_rn(sg, __fmaf_rn(g[c], __fmaf_rn(-1.f, sg, 1.f), 1.f));
+      dg[c] = __fmul_rn(__fmul_rn(dv[c], hat[c]), q);
+    }
   }
 }
 

@@ -96,11 +96,10 @@ __device__ __forceinline__ void decode_token(const FwdParams& p, const TokenLoad
   }
   if (NORM != kNormNone) apply_norm<NORM, NV, GV>(acc, p.G, lpg, p.eps);
   if (p.g != nullptr) {
+    float gf[NV];
 #pragma unroll
-    for (int c = 0; c < NV; ++c) {
-      const float gf = to_f(tok.g.v[c]);
-      acc[c] = acc[c] * (gf * sigmoidf_(gf));
-    }
+    for (int c = 0; c < NV; ++c) gf[c] = to_f(tok.g.v[c]);
+    gate_pairs<NV>(acc, gf);
   }
   if (active) {
     Pack<T, NV> o;

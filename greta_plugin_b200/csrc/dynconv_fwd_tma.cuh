@@ -584,12 +584,14 @@ __global__ void __launch_bounds__(32 + fwd_rows_max_channels(WT) / kVec, 1)
         if (gg != nullptr) {
           const PX gv = *reinterpret_cast<const PX*>(gsp);
           const PX gw = *reinterpret_cast<const PX*>(gsp + rowx);
+          float gf[NV], gn[NV];
 #pragma unroll
           for (int c = 0; c < NV; ++c) {
-            const float gf = to_f(gv.v[c]), gn = to_f(gw.v[c]);
-            acc[c] = acc[c] * (gf * sigmoidf_(gf));
-            acn[c] = acn[c] * (gn * sigmoidf_(gn));
+            gf[c] = to_f(gv.v[c]);
+            gn[c] = to_f(gw.v[c]);
           }
+          gate_pairs<NV>(acc, gf);
+          gate_pairs<NV>(acn, gn);
         }
         {
           PX o, q;
@@ -631,11 +633,10 @@ __global__ void __launch_bounds__(32 + fwd_rows_max_channels(WT) / kVec, 1)
       }
       if (gg != nullptr) {
         const PX gv = *reinterpret_cast<const PX*>(gsp);
+        float gf[NV];
 #pragma unroll
-        for (int c = 0; c < NV; ++c) {
-          const float gf = to_f(gv.v[c]);
-          acc[c] = acc[c] * (gf * sigmoidf_(gf));
-        }
+        for (int c = 0; c < NV; ++c) gf[c] = to_f(gv.v[c]);
+        gate_pairs<NV>(acc, gf);
       }
       {
         PX o;

@@ -264,6 +264,9 @@ def test_inference_channel_split(capi):
     (4096, 4, 1, True, True, torch.bfloat16, [257, 2, 400]),
     (2048, 7, 128, True, True, torch.bfloat16, [1, 6, 7, 8, 5000, 0]),  # 1 slice, producer in warp 0
     (4096, 7, 128, False, True, torch.bfloat16, [3000, 1, 999]),         # 2 slices, producer in warp 0
+    # many short requests of odd and even lengths: tokens in pairs and alone
+    (2048, 7, 64, True, True, torch.bfloat16, [2, 3, 1, 4, 9, 10, 11, 2, 1, 13, 40, 7, 8, 0, 5, 6, 300]),
+    (2048, 7, 128, False, True, torch.bfloat16, [1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12, 13, 14, 15, 160]),
     (4096, 7, 8, True, False, torch.bfloat16, [2000, 50]),               # the same, filters per tap
     (2048, 7, 2, False, False, torch.bfloat16, [700, 5, 300]),           # 2 slices of 1024, producer warp
     (1024, 7, 16, False, True, torch.float16, [30, 31, 200]),
