@@ -362,7 +362,7 @@ def run_decode(torch, vc, dev, args, dist, rank, world, peak, traffic):
 
 
 def run_channel_split(torch, vc, dev, args, dist, rank, world, peak):
-    """Multi-GPU mode of the north star: the channels of ONE batch split over
+    """Channel-split multi-GPU mode: the channels of ONE batch split over
     the ranks in contiguous, group-aligned shards (vLLM's column-parallel
     layout, greta_plugin_b200.sharding.channel_shard); every rank runs the
     kernels on its D/N channels of the same tokens, with no collective on the
